@@ -1,0 +1,123 @@
+/*
+ * exactsample_b200: C ABI of the B200 (sm_100a) sampling and speculative-
+ * verification kernels.
+ *
+ * This header replaces the reference's C++ ABI
+ *   include/exactsample/api.h:7-44   (Status, Path, DType, Matrix, Vector,
+ *                                     RowResult, Arguments, workspace_size,
+ *                                     exactsample::launch)
+ * and the argument checks of its torch binding
+ *   csrc/bindings.cpp:45-136          (verify_out: dtype, rank, capacity,
+ *                                     alignment and aliasing checks)
+ * with plain C: every tensor is a pointer plus sizes and strides (in
+ * elements), and every error is a negative return code with a message.
+ *
+ * Semantics are those of the exactsample decoding contract v1.0
+ * (docs/contract.md, docs/rng.md of the reference): per-request statuses,
+ * tokens -1 on failure, Philox4x32-10 at (seed, stream, position, substream,
+ * token / 4).
+ *
+ * Ownership and threading: every buffer is caller-owned device memory on the
+ * current CUDA device; es_verify only enqueues kernels on `stream` and never
+ * allocates or synchronizes. One call at a time may use a given workspace
+ * (calls on one stream are ordered; overlapping calls on different streams
+ * that share a workspace race).
+ */
+#ifndef EXACTSAMPLE_B200_H
+#define EXACTSAMPLE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ES_ABI_VERSION 1
+
+/* Per-request status (api.h:7, docs/contract.md "Shapes and failure boundaries"). */
+enum es_status { ES_OK = 0, ES_NO_VALID_TOKEN = 1, ES_INVALID_INPUT = 2, ES_DRAFT_ZERO_PROB = 3 };
+/* path_used values (api.h:8). */
+enum es_path { ES_PATH_REFERENCE = 0, ES_PATH_FUSED = 1 };
+/* Element types (api.h:9 for the logits; the rest name the other tensors). */
+enum es_dtype { ES_F32 = 0, ES_F64 = 1, ES_F16 = 2, ES_BF16 = 3, ES_I32 = 4, ES_I64 = 5, ES_U8 = 6 };
+/* Verification mode and dispatch (api.h:32; cuda.py:149-150). */
+enum es_mode { ES_RATIO = 0, ES_COUPLED = 1 };
+enum es_dispatch { ES_AUTO = 0, ES_REFERENCE = 1, ES_FUSED = 2 };
+
+/* Return codes. Structural problems are reported before anything is
+ * enqueued; per-request numerical problems are statuses, not errors. */
+enum es_error {
+  ES_SUCCESS = 0,
+  ES_ERR_ARGUMENT = -1,    /* a tensor has the wrong dtype, rank, shape or a negative stride */
+  ES_ERR_CAPACITY = -2,    /* workspace or output too small */
+  ES_ERR_ALIGNMENT = -3,   /* workspace not 8-byte aligned */
+  ES_ERR_ALIAS = -4,       /* an output overlaps an input or another output */
+  ES_ERR_UNSUPPORTED = -5, /* a shape this build does not handle (e.g. vocab too large for one cluster) */
+  ES_ERR_LAUNCH = -6,      /* a CUDA launch failed (message has cudaGetErrorString) */
+  ES_ERR_DEVICE = -7       /* the current device is not an sm_100 GPU */
+};
+
+/* A strided view of at most two dimensions; sizes and strides in elements.
+ * A 1-D tensor uses size[0] / stride[0]. data == NULL marks an absent
+ * optional tensor (draft_logits, mask). */
+typedef struct es_tensor {
+  void* data;
+  int64_t size[2];
+  int64_t stride[2];
+  int32_t dtype; /* enum es_dtype */
+  int32_t ndim;
+} es_tensor;
+
+/* The arguments of one call (api.h:20-35 Arguments; bindings.cpp:139-146
+ * schema of exactsample::verify_out, in the same order). */
+typedef struct es_args {
+  es_tensor target_logits; /* f32/f64/f16/bf16 [rows, vocab] */
+  es_tensor cu_rows;       /* i64 [requests + 1] */
+  es_tensor draft_ids;     /* i64 [requests, >= max_draft] */
+  es_tensor draft_logits;  /* optional, target dtype and shape */
+  es_tensor temperature;   /* f64 [requests] */
+  es_tensor top_k;         /* i64 [requests], 0 disables */
+  es_tensor top_p;         /* f64 [requests] */
+  es_tensor min_p;         /* f64 [requests] */
+  es_tensor draft_kind;    /* i64 [requests], 0 one-hot, 1 full */
+  es_tensor seeds;         /* i64 [requests], uint64 bits */
+  es_tensor stream_ids;    /* i64 [requests], [0, 2^32) */
+  es_tensor positions;     /* i64 [rows], [0, 2^32) */
+  es_tensor mask;          /* optional i32 [rows, ceil(vocab / 32)] */
+  es_tensor workspace;     /* u8 [>= es_workspace_bytes], contiguous, 8-byte aligned */
+  es_tensor tokens;        /* out i64 [>= requests, >= max_draft + 1] */
+  es_tensor accepted_len;  /* out i32 [>= requests] */
+  es_tensor status;        /* out i32 [>= requests] */
+  es_tensor path_used;     /* out i32 [>= requests] */
+  int64_t mode;            /* enum es_mode */
+  int64_t dispatch;        /* enum es_dispatch */
+  int64_t max_draft;
+  int64_t list_max;        /* [0, 256]: largest kept set processed as an FP64 list; 0 skips lists */
+} es_args;
+
+/* Workspace bytes for `rows` target rows (api.h:39-43 workspace_size, and
+ * cuda.py:89): 8 + rows * (32 + max(12288, 20 * vocab if reference)). */
+int es_workspace_bytes(int64_t rows, int64_t vocab, int32_t reference, uint64_t* bytes);
+
+/* Validates the arguments and enqueues the call on `stream` (a
+ * cudaStream_t; NULL is the legacy default stream). Replaces
+ * exactsample::launch (api.h:44, csrc/verify/verify.cu:220-228) together
+ * with the checks of bindings.cpp:50-119. */
+int es_verify(const es_args* args, void* stream);
+
+/* The same call, with `before` and `after` (cudaEvent_t, either may be NULL)
+ * recorded on `stream` immediately around the row kernel. Measurement only:
+ * it exists so that benchmarks can time the dominant kernel by itself. */
+int es_verify_timed(const es_args* args, void* stream, void* before, void* after);
+
+/* The message of the last error returned on this thread ("" after success). */
+const char* es_last_error(void);
+
+/* ES_ABI_VERSION of the loaded library. */
+int es_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXACTSAMPLE_B200_H */
