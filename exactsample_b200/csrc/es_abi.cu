@@ -1,0 +1,328 @@
+// The C ABI (include/exactsample_b200.h): argument validation, workspace
+// sizing, cluster sizing and the launch sequence of one call.
+//
+// The checks and their messages follow the reference's torch binding
+// (csrc/bindings.cpp:50-119), so a caller sees the same errors whether it
+// comes through the torch op or calls this library directly.
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <numeric>
+#include <string>
+
+#include "es_kernel.cuh"
+
+namespace es {
+// One block validates cu_rows for very large batches (the preparation
+// kernel's blocks then read the flag instead of re-checking every offset).
+__global__ void __launch_bounds__(1024) check_offsets(const __grid_constant__ Params p) {
+  const bool bad = offsets_malformed(p);
+  if (threadIdx.x == 0) *malformed_flag(p.workspace) = bad;
+}
+
+// One thread per request: outputs reset to the failed state (tokens -1,
+// accepted 0), metadata status, path, and the request's arrival counter.
+__global__ void __launch_bounds__(128) prepare(const __grid_constant__ Params p) {
+  allow_dependent_grid();  // the row kernel may launch now and start loading logits
+  bool bad;
+  if (p.offsets_inline) {
+    bad = offsets_malformed(p);
+  } else {
+    bad = *malformed_flag(p.workspace) != 0;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (p.offsets_inline) *malformed_flag(p.workspace) = bad;
+    *fallback_count(p.workspace) = 0;
+  }
+  if (p.rows > 0 && blockIdx.x == 0) {
+    uint32_t* d = reinterpret_cast<uint32_t*>(diagnostics(p.workspace, p.rows));
+    for (int i = threadIdx.x; i < int(sizeof(Diagnostics) / 4); i += blockDim.x) d[i] = 0;
+  }
+  const int64_t req = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (req >= p.requests) return;
+  for (int64_t i = 0; i <= p.max_draft; ++i) p.tokens[req * p.tok_s0 + i * p.tok_s1] = -1;
+  p.accepted[req * p.acc_s] = 0;
+  p.path[req * p.path_s] = p.exact_draws ? ES_PATH_REFERENCE : ES_PATH_FUSED;
+  const int32_t status = bad ? ES_INVALID_INPUT : metadata_status(p, req);
+  p.status[req * p.st_s] = status;
+  if (status == ES_OK) arrivals(p.workspace, p.rows)[at(p.cu_rows, p.cu_s, req)] = 0;
+}
+
+template <int DT> cudaError_t launch_rows(const Params& p, int cluster, cudaStream_t stream);
+extern template cudaError_t launch_rows<ES_F32>(const Params&, int, cudaStream_t);
+extern template cudaError_t launch_rows<ES_F64>(const Params&, int, cudaStream_t);
+extern template cudaError_t launch_rows<ES_F16>(const Params&, int, cudaStream_t);
+extern template cudaError_t launch_rows<ES_BF16>(const Params&, int, cudaStream_t);
+}  // namespace es
+
+namespace {
+using es::Params;
+
+thread_local std::string g_error;
+
+int fail(int code, const std::string& message) {
+  g_error = message;
+  return code;
+}
+
+size_t element_size(int32_t dtype) {
+  switch (dtype) {
+    case ES_F32: case ES_I32: return 4;
+    case ES_F64: case ES_I64: return 8;
+    case ES_F16: case ES_BF16: return 2;
+    case ES_U8: return 1;
+    default: return 0;
+  }
+}
+int64_t numel(const es_tensor& t) {
+  int64_t n = 1;
+  for (int d = 0; d < t.ndim; ++d) n *= t.size[d];
+  return n;
+}
+// [first byte, one past the last byte] of a strided view.
+bool extent(const es_tensor& t, uintptr_t* begin, uintptr_t* end) {
+  if (numel(t) == 0) return false;
+  const size_t e = element_size(t.dtype);
+  uintptr_t span = e;
+  for (int d = 0; d < t.ndim; ++d) span += uintptr_t(t.size[d] - 1) * uintptr_t(t.stride[d]) * e;
+  *begin = reinterpret_cast<uintptr_t>(t.data);
+  *end = *begin + span;
+  return true;
+}
+// Address intervals prove disjointness (bindings.cpp:25-37).
+bool disjoint(const es_tensor& a, const es_tensor& b) {
+  uintptr_t a0, a1, b0, b1;
+  if (!extent(a, &a0, &a1) || !extent(b, &b0, &b1)) return true;
+  return a1 <= b0 || b1 <= a0;
+}
+// A view whose elements never share an address (bindings.cpp:38-44).
+bool no_internal_overlap(const es_tensor& t) {
+  if (numel(t) <= 1) return true;
+  for (int d = 0; d < t.ndim; ++d)
+    if (t.size[d] > 1 && t.stride[d] == 0) return false;
+  if (t.ndim == 1 || t.size[0] <= 1 || t.size[1] <= 1) return true;
+  const int64_t divisor = std::gcd(t.stride[0], t.stride[1]);
+  return t.size[0] <= t.stride[1] / divisor || t.size[1] <= t.stride[0] / divisor;
+}
+bool check(const es_tensor& t, int32_t dtype, int ndim, const char* name) {
+  if (t.data == nullptr || t.dtype != dtype || t.ndim != ndim) {
+    g_error = std::string(name) + " has wrong device, dtype or rank";
+    return false;
+  }
+  for (int d = 0; d < ndim; ++d)
+    if (t.stride[d] < 0 || t.size[d] < 0) {
+      g_error = std::string(name) + " has a negative stride";
+      return false;
+    }
+  return true;
+}
+bool is_logit_dtype(int32_t d) { return d == ES_F32 || d == ES_F64 || d == ES_F16 || d == ES_BF16; }
+
+// Cluster ranks per row: about TOKENS_PER_RANK tokens per rank, more ranks for
+// small batches (a single row spreads over 16 SMs), and at most MAX_SLICE
+// bytes of shared memory per rank.
+constexpr int64_t TOKENS_PER_RANK = 19000;
+constexpr size_t MAX_SMEM = 227 * 1024;
+
+int choose_cluster(int64_t rows, int64_t vocab, int dtype, int* slice_words, size_t* smem) {
+  const int64_t words = (vocab + 31) / 32;
+  int c = int(std::min<int64_t>(16, std::max<int64_t>(1, (vocab + TOKENS_PER_RANK - 1) / TOKENS_PER_RANK)));
+  if (rows <= 16 && vocab >= 4096) c = 16;
+  else if (rows <= 48 && vocab >= 4096) c = std::max(c, 8);
+  // EXACTSAMPLE_CLUSTER=n asks for n ranks per row (1..16), e.g. to show that
+  // results do not depend on the split; shared memory limits may raise it.
+  if (const char* forced = std::getenv("EXACTSAMPLE_CLUSTER")) {
+    const int n = std::atoi(forced);
+    if (n >= 1 && n <= 16) c = n;
+  }
+  auto bytes = [&](int sw) {
+    switch (dtype) {
+      case ES_F32: return es::smem_bytes<ES_F32>(sw);
+      case ES_F64: return es::smem_bytes<ES_F64>(sw);
+      case ES_F16: return es::smem_bytes<ES_F16>(sw);
+      default: return es::smem_bytes<ES_BF16>(sw);
+    }
+  };
+  for (;; ++c) {
+    if (c > 16) return -1;
+    const int sw = int((words + c - 1) / c);
+    const int used = int((words + sw - 1) / sw);  // no empty ranks
+    if (bytes(sw) <= MAX_SMEM) {
+      *slice_words = sw;
+      *smem = bytes(sw);
+      return used;
+    }
+  }
+}
+
+int device_check() {
+  static thread_local int checked_device = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(ES_ERR_DEVICE, "no CUDA device is available");
+  if (dev == checked_device) return ES_SUCCESS;
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess || major != 10)
+    return fail(ES_ERR_DEVICE, "exactsample_b200 requires an sm_100 (B200) GPU");
+  checked_device = dev;
+  return ES_SUCCESS;
+}
+
+int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaEvent_t after) {
+  g_error.clear();
+  if (a == nullptr) return fail(ES_ERR_ARGUMENT, "null arguments");
+  const es_tensor& logits = a->target_logits;
+  if (logits.data == nullptr || logits.ndim != 2) return fail(ES_ERR_ARGUMENT, "target_logits must be a 2D CUDA tensor");
+  if (!is_logit_dtype(logits.dtype))
+    return fail(ES_ERR_ARGUMENT, "exactsample logits require float16/bfloat16/float32/float64");
+  if (logits.stride[0] < 0 || logits.stride[1] < 0) return fail(ES_ERR_ARGUMENT, "target_logits has a negative stride");
+  if (!check(a->cu_rows, ES_I64, 1, "cu_rows")) return ES_ERR_ARGUMENT;
+  if (a->cu_rows.size[0] < 1) return fail(ES_ERR_ARGUMENT, "cu_rows must contain an endpoint");
+  const int64_t requests = a->cu_rows.size[0] - 1, rows = logits.size[0], vocab = logits.size[1];
+  if (requests == 0 && rows != 0) return fail(ES_ERR_ARGUMENT, "an empty request batch cannot contain target rows");
+  if (!(vocab > 0 && vocab <= INT32_MAX && rows <= INT32_MAX && requests <= INT32_MAX))
+    return fail(ES_ERR_ARGUMENT, "exactsample dimensions exceed int32 kernel indexing");
+  if (rows > 65535) return fail(ES_ERR_ARGUMENT, "exactsample supports at most 65535 target rows per call");
+  if (!(a->max_draft >= 0 && a->max_draft < INT32_MAX)) return fail(ES_ERR_ARGUMENT, "invalid max_draft");
+  if (!(a->mode >= 0 && a->mode <= 1 && a->dispatch >= 0 && a->dispatch <= 2))
+    return fail(ES_ERR_ARGUMENT, "invalid mode/dispatch");
+  if (!(a->list_max >= 0 && a->list_max <= 256)) return fail(ES_ERR_ARGUMENT, "list_max must be in [0, 256]");
+  if (!check(a->draft_ids, ES_I64, 2, "draft_ids")) return ES_ERR_ARGUMENT;
+  if (!(a->draft_ids.size[0] == requests && a->draft_ids.size[1] >= a->max_draft))
+    return fail(ES_ERR_ARGUMENT, "draft_ids capacity mismatch");
+  const es_tensor* fp[3] = {&a->temperature, &a->top_p, &a->min_p};
+  for (const es_tensor* t : fp) {
+    if (!check(*t, ES_F64, 1, "floating request parameter")) return ES_ERR_ARGUMENT;
+    if (t->size[0] != requests) return fail(ES_ERR_ARGUMENT, "request parameter length mismatch");
+  }
+  const es_tensor* ip[4] = {&a->top_k, &a->draft_kind, &a->seeds, &a->stream_ids};
+  for (const es_tensor* t : ip) {
+    if (!check(*t, ES_I64, 1, "integer request parameter")) return ES_ERR_ARGUMENT;
+    if (t->size[0] != requests) return fail(ES_ERR_ARGUMENT, "request parameter length mismatch");
+  }
+  if (!check(a->positions, ES_I64, 1, "positions")) return ES_ERR_ARGUMENT;
+  if (a->positions.size[0] != rows) return fail(ES_ERR_ARGUMENT, "positions must be per target row");
+  const bool has_draft = a->draft_logits.data != nullptr, has_mask = a->mask.data != nullptr;
+  if (has_draft) {
+    const es_tensor& q = a->draft_logits;
+    if (q.ndim != 2 || q.size[0] != rows || q.size[1] != vocab || q.stride[0] < 0 || q.stride[1] < 0)
+      return fail(ES_ERR_ARGUMENT, "draft_logits shape/device mismatch");
+    if (q.dtype != logits.dtype) return fail(ES_ERR_ARGUMENT, "draft_logits must have the target_logits dtype");
+  }
+  if (has_mask) {
+    if (!check(a->mask, ES_I32, 2, "mask")) return ES_ERR_ARGUMENT;
+    if (!(a->mask.size[0] == rows && a->mask.size[1] == (vocab + 31) / 32))
+      return fail(ES_ERR_ARGUMENT, "mask shape mismatch");
+  }
+  const es_tensor& ws = a->workspace;
+  if (!check(ws, ES_U8, 1, "workspace")) return ES_ERR_ARGUMENT;
+  if (!(ws.stride[0] == 1 || ws.size[0] <= 1)) return fail(ES_ERR_ARGUMENT, "workspace must be contiguous");
+  if (uint64_t(rows) > uint64_t(INT64_MAX - 8) / (sizeof(es::RowResult) + uint64_t(vocab) * 20))
+    return fail(ES_ERR_ARGUMENT, "workspace size overflow");
+  uint64_t need = 0;
+  es_workspace_bytes(rows, vocab, a->dispatch == ES_REFERENCE, &need);
+  if (uint64_t(ws.size[0]) < need)
+    return fail(ES_ERR_CAPACITY, a->dispatch == ES_REFERENCE
+                                     ? "workspace capacity exceeded (the reference path needs a plan made with reference=True)"
+                                     : "workspace capacity exceeded");
+  if (reinterpret_cast<uintptr_t>(ws.data) % 8 != 0) return fail(ES_ERR_ALIGNMENT, "workspace alignment must be 8 bytes");
+  if (!check(a->tokens, ES_I64, 2, "tokens")) return ES_ERR_ARGUMENT;
+  if (!(a->tokens.size[0] >= requests && a->tokens.size[1] >= a->max_draft + 1))
+    return fail(ES_ERR_CAPACITY, "tokens capacity exceeded");
+  const es_tensor* small[3] = {&a->accepted_len, &a->status, &a->path_used};
+  for (const es_tensor* t : small) {
+    if (!check(*t, ES_I32, 1, "output")) return ES_ERR_ARGUMENT;
+    if (t->size[0] < requests) return fail(ES_ERR_CAPACITY, "output capacity exceeded");
+  }
+  const es_tensor* inputs[13] = {&logits, &a->cu_rows, &a->draft_ids, &a->temperature, &a->top_k, &a->top_p,
+                                 &a->min_p, &a->draft_kind, &a->seeds, &a->stream_ids, &a->positions,
+                                 has_draft ? &a->draft_logits : nullptr, has_mask ? &a->mask : nullptr};
+  const es_tensor* outputs[5] = {&ws, &a->tokens, &a->accepted_len, &a->status, &a->path_used};
+  for (int i = 0; i < 5; ++i) {
+    if (!no_internal_overlap(*outputs[i])) return fail(ES_ERR_ALIAS, "output has overlapping strides");
+    for (const es_tensor* in : inputs)
+      if (in != nullptr && !disjoint(*outputs[i], *in))
+        return fail(ES_ERR_ALIAS, "exactsample input/output aliasing is forbidden");
+    for (int j = 0; j < i; ++j)
+      if (!disjoint(*outputs[i], *outputs[j])) return fail(ES_ERR_ALIAS, "exactsample outputs alias");
+  }
+  if (requests == 0) return ES_SUCCESS;
+  const int dev = device_check();
+  if (dev != ES_SUCCESS) return dev;
+
+  Params p{};
+  p.target = logits.data; p.t_s0 = logits.stride[0]; p.t_s1 = logits.stride[1];
+  if (has_draft) { p.draft = a->draft_logits.data; p.q_s0 = a->draft_logits.stride[0]; p.q_s1 = a->draft_logits.stride[1]; }
+  p.cu_rows = static_cast<const int64_t*>(a->cu_rows.data); p.cu_s = a->cu_rows.stride[0];
+  p.draft_ids = static_cast<const int64_t*>(a->draft_ids.data);
+  p.d_s0 = a->draft_ids.stride[0]; p.d_s1 = a->draft_ids.stride[1];
+  p.temperature = static_cast<const double*>(a->temperature.data); p.temp_s = a->temperature.stride[0];
+  p.top_k = static_cast<const int64_t*>(a->top_k.data); p.topk_s = a->top_k.stride[0];
+  p.top_p = static_cast<const double*>(a->top_p.data); p.topp_s = a->top_p.stride[0];
+  p.min_p = static_cast<const double*>(a->min_p.data); p.minp_s = a->min_p.stride[0];
+  p.draft_kind = static_cast<const int64_t*>(a->draft_kind.data); p.kind_s = a->draft_kind.stride[0];
+  p.seeds = static_cast<const int64_t*>(a->seeds.data); p.seed_s = a->seeds.stride[0];
+  p.streams = static_cast<const int64_t*>(a->stream_ids.data); p.stream_s = a->stream_ids.stride[0];
+  p.positions = static_cast<const int64_t*>(a->positions.data); p.pos_s = a->positions.stride[0];
+  if (has_mask) { p.mask = static_cast<const int32_t*>(a->mask.data); p.m_s0 = a->mask.stride[0]; p.m_s1 = a->mask.stride[1]; }
+  p.workspace = static_cast<uint8_t*>(ws.data);
+  p.tokens = static_cast<int64_t*>(a->tokens.data); p.tok_s0 = a->tokens.stride[0]; p.tok_s1 = a->tokens.stride[1];
+  p.accepted = static_cast<int32_t*>(a->accepted_len.data); p.acc_s = a->accepted_len.stride[0];
+  p.status = static_cast<int32_t*>(a->status.data); p.st_s = a->status.stride[0];
+  p.path = static_cast<int32_t*>(a->path_used.data); p.path_s = a->path_used.stride[0];
+  p.rows = int32_t(rows); p.requests = int32_t(requests); p.vocab = int32_t(vocab);
+  p.max_draft = int32_t(a->max_draft); p.mode = int32_t(a->mode); p.dispatch = int32_t(a->dispatch);
+  p.exact_draws = a->dispatch == ES_REFERENCE;
+  p.list_max = p.exact_draws ? 0 : int32_t(a->list_max);
+  p.offsets_inline = requests <= 8192;
+
+  int cluster = 1;
+  size_t smem = 0;
+  if (rows > 0) {
+    cluster = choose_cluster(rows, vocab, logits.dtype, &p.slice_words, &smem);
+    if (cluster < 0) return fail(ES_ERR_UNSUPPORTED, "vocabulary too large for one 16-block cluster's shared memory");
+    const size_t e = element_size(logits.dtype);
+    p.vector_load = logits.stride[1] == 1 && reinterpret_cast<uintptr_t>(logits.data) % 16 == 0 &&
+                    (uint64_t(logits.stride[0]) * e) % 16 == 0;
+  }
+  cudaGetLastError();  // clear a stale error so the checks below report this call's launches
+  if (!p.offsets_inline) es::check_offsets<<<1, 1024, 0, stream>>>(p);
+  es::prepare<<<unsigned((requests + 127) / 128), 128, 0, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess && rows > 0) {
+    if (before != nullptr) cudaEventRecord(before, stream);
+    switch (logits.dtype) {
+      case ES_F32: e = es::launch_rows<ES_F32>(p, cluster, stream); break;
+      case ES_F64: e = es::launch_rows<ES_F64>(p, cluster, stream); break;
+      case ES_F16: e = es::launch_rows<ES_F16>(p, cluster, stream); break;
+      default: e = es::launch_rows<ES_BF16>(p, cluster, stream); break;
+    }
+    if (after != nullptr) cudaEventRecord(after, stream);
+  }
+  if (e != cudaSuccess) return fail(ES_ERR_LAUNCH, std::string("exactsample kernel launch failed: ") + cudaGetErrorString(e));
+  return ES_SUCCESS;
+}
+}  // namespace
+
+extern "C" {
+
+int es_workspace_bytes(int64_t rows, int64_t vocab, int32_t reference, uint64_t* bytes) {
+  if (rows < 0 || vocab < 1 || bytes == nullptr) return fail(ES_ERR_ARGUMENT, "invalid workspace shape");
+  const uint64_t scratch = reference ? uint64_t(vocab) * 20 : 0;
+  *bytes = 8 + uint64_t(rows) * (32 + (scratch > 12288 ? scratch : 12288));
+  return ES_SUCCESS;
+}
+
+int es_verify(const es_args* args, void* stream) {
+  return verify_impl(args, static_cast<cudaStream_t>(stream), nullptr, nullptr);
+}
+
+int es_verify_timed(const es_args* args, void* stream, void* before, void* after) {
+  return verify_impl(args, static_cast<cudaStream_t>(stream), static_cast<cudaEvent_t>(before),
+                     static_cast<cudaEvent_t>(after));
+}
+
+const char* es_last_error(void) { return g_error.c_str(); }
+
+int es_abi_version(void) { return ES_ABI_VERSION; }
+
+}  // extern "C"

@@ -1,0 +1,344 @@
+// The row kernel's body (one cluster per row) and its launcher.
+#pragma once
+#include "es_rows.cuh"
+
+namespace es {
+
+constexpr uint32_t BULK_CHUNK = 16384;  // bytes per TMA bulk copy
+constexpr uint32_t WAIT_LIMIT = 1u << 26;  // mbarrier polls before a copy is declared lost
+
+__host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+template <int DT> __host__ __device__ constexpr size_t smem_head() {
+  return align_up(sizeof(Smem<typename Types<DT>::W>), 128);
+}
+template <int DT> __host__ __device__ constexpr size_t smem_bytes(int slice_words) {
+  return smem_head<DT>() + align_up(4 * size_t(slice_words), 128) +
+         align_up(size_t(slice_words) * 32 * sizeof(typename Types<DT>::T), 128);
+}
+
+// The last request whose segment starts at or before `row` (empty segments
+// share their start with the next request, which owns the row).
+__device__ inline int request_of(const Params& p, int row) {
+  int lo = 0, hi = p.requests - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) / 2;
+    if (at(p.cu_rows, p.cu_s, mid) <= row) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+template <int DT> struct RowKernel {
+  using R = Row<DT>;
+  using T = typename R::T;
+  using W = typename R::W;
+  using Key = typename R::Key;
+
+  // Target point mass at the greedy token (temperature 0).
+  __device__ static void greedy(R& r, const RowCtx& c, bool verify, bool full_q, double sq, RowResult& res) {
+    const int g = r.all.b1i;
+    res.sample = g;
+    if (!verify) return;
+    res.accept = c.draft_id == g;
+    if (res.accept) return;
+    if (!full_q) {
+      res.residual = g;
+      return;
+    }
+    // max(p - q, 0) is positive only at the greedy token, unless q rounds to 1 there.
+    const W y = r.q_value(g);
+    const double q = y > W(-INFINITY) ? exp(double(y) - double(r.all.qmax)) / sq : 0.0;
+    res.residual = 1.0 - q > 0 ? g : -1;
+  }
+
+  // q of the draft token (1 for one-hot drafts).
+  __device__ static double q_of_draft(R& r, const RowCtx& c, bool full_q, double sq) {
+    if (!full_q) return 1.0;
+    const W y = r.q_value(c.draft_id);
+    return y > W(-INFINITY) ? exp(double(y) - double(r.all.qmax)) / sq : 0.0;
+  }
+
+  // Rank 0 finishes a list row: the m gathered candidates hold the kept
+  // n_keep tokens first once sorted. Oracle formulas throughout (FP64).
+  __device__ static void list_finish(R& r, const RowCtx& c, int m, int n_keep, bool verify, bool full_q, double sq,
+                                     double u_accept, RowResult& res) {
+    auto& s = r.s;
+    r.sort_candidates(m);
+    const int i = threadIdx.x;
+    const bool in = i < n_keep;
+    const int id = in ? s.u.cand.id[i] : INT_MAX;
+    double w = 0;
+    bool ok = false;
+    if (in) {
+      const W v = key_value(Key(s.u.cand.key[i]));
+      w = exp(r.x64(v));
+      ok = w >= r.min_p && w > 0;
+    }
+    // min-p and positivity remove a suffix of the order.
+    const int first_out = block_all(in && !ok ? i : INT_MAX, [](int a, int b) { return a < b ? a : b; }, s.red.ints);
+    const int n1 = min(n_keep, first_out);
+    const u128 f = i < n1 ? fx_of(w) : u128(0);
+    u128 total;
+    const u128 prefix = block_scan(f, s.red.fxs, &total);
+    bool near;
+    const double d1 = fx_round(total, uint32_t(n1), &near);
+    r.count_near_tie(near);
+    int n2 = n1;
+    double denominator = d1;
+    if (r.top_p < 1) {
+      const double target = r.top_p * d1;
+      if (target <= 1.0) {
+        n2 = 1;  // the first token's weight is exactly 1
+      } else {
+        bool nr = false;
+        const bool reach = i < n1 && fx_reaches(prefix, uint32_t(i + 1), target, &nr);
+        const int first = block_all(reach ? i : INT_MAX, [](int a, int b) { return a < b ? a : b; }, s.red.ints);
+        n2 = first == INT_MAX ? n1 : first + 1;
+      }
+      if (i == n2 - 1) s.fxval = prefix;
+      __syncthreads();
+      denominator = fx_round(s.fxval, uint32_t(n2), &near);
+      r.count_near_tie(near);
+      __syncthreads();
+    }
+    const double prob = i < n2 ? w / denominator : 0.0;
+    if (i < LIST_MAX) s.lp[i] = prob;
+    __syncthreads();
+    // One draw over the list: argmax log(p) + G, lowest ID on ties.
+    auto draw_list = [&](uint32_t sub, int excluded) {
+      Best b = no_best();
+      if (i < n2 && id != excluded && prob > 0) b = Best{log(prob) + noise64(r.addr.word(sub, uint32_t(id))), id};
+      b = block_all(b, [](Best a, Best c2) { return best_of(a, c2); }, s.red.bests);
+      return b.id == INT_MAX ? -1 : b.id;
+    };
+    if (!verify) {
+      res.sample = draw_list(0, -1);
+      return;
+    }
+    const int at_draft = block_all(i < n2 && id == c.draft_id ? i : INT_MAX, [](int a, int b) { return a < b ? a : b; },
+                                   s.red.ints);
+    const double px = at_draft == INT_MAX ? 0.0 : s.lp[at_draft];
+    const double qx = q_of_draft(r, c, full_q, sq);
+    res.accept = u_accept < fmin(1.0, px / qx);
+    if (res.accept) return;
+    if (!full_q) {
+      res.residual = draw_list(2, c.draft_id);
+      return;
+    }
+    Best b = no_best();
+    if (i < n2 && prob > 0) {
+      const W y = r.q_value(id);
+      const double q = y > W(-INFINITY) ? exp(double(y) - double(r.all.qmax)) / sq : 0.0;
+      const double rr = fmax(prob - q, 0.0);
+      if (rr > 0) b = Best{log(rr) + noise64(r.addr.word(2, uint32_t(id))), id};
+    }
+    b = block_all(b, [](Best a, Best c2) { return best_of(a, c2); }, s.red.bests);
+    res.residual = b.id == INT_MAX ? -1 : b.id;
+  }
+
+  __device__ static void positive(R& r, const RowCtx& c, bool verify, bool full_q, double sq, RowResult& res,
+                                  const Params& p) {
+    const int valid = r.all.valid;
+    const int64_t k = c.top_k;
+    const int n_keep = (k > 0 && k < valid) ? int(k) : valid;
+    const int list_max = p.exact_draws ? 0 : min(p.list_max, LIST_MAX);
+    const double u_accept = uniform64(r.addr.word(1, 0));
+    if (n_keep <= list_max) {
+      int m;
+      if (n_keep < valid) {
+        m = r.gather_window(n_keep);
+        if (m < 0) {
+          const Cut<Key> cut = r.select_nth(n_keep, [](Key, int, W) { return true; });
+          m = r.gather_all([&](W v, int t) { return cut.keeps(order_key(v), t); });
+        }
+      } else {
+        m = r.gather_all([](W, int) { return true; });
+      }
+      if (r.rank == 0) list_finish(r, c, m, n_keep, verify, full_q, sq, u_accept, res);
+      return;
+    }
+    Cut<Key> cut_k{0, 0, 0}, cut_p{0, 0, 0};
+    if (k > 0 && k < valid) cut_k = r.select_nth(int(k), [](Key, int, W) { return true; });
+    double sp = 0;
+    bool sp_known = false;
+    if (r.top_p < 1) {
+      cut_p = r.top_p_cut(cut_k, &sp);
+      sp_known = true;
+    }
+    auto kept = [cut_k, cut_p](Key key, int t) { return cut_k.keeps(key, t) && cut_p.keeps(key, t); };
+    if (!verify) {
+      res.sample = r.draw(0, -1, kept, p.exact_draws != 0);
+      return;
+    }
+    if (!sp_known) sp = r.exact_mass(kept);
+    const int x = c.draft_id;
+    double px = 0;
+    if (r.valid_global(x)) {
+      const W v = r.value_global(x);
+      if (kept(order_key(v), x)) {
+        const double w = exp(r.x64(v));
+        if (w >= r.min_p && w > 0) px = w / sp;
+      }
+    }
+    res.accept = u_accept < fmin(1.0, px / q_of_draft(r, c, full_q, sq));
+    if (res.accept) return;
+    res.residual = full_q ? r.draw_residual_q(kept, sp, sq) : r.draw(2, x, kept, p.exact_draws != 0);
+  }
+};
+
+template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const __grid_constant__ Params p) {
+  using K = RowKernel<DT>;
+  using R = typename K::R;
+  using T = typename K::T;
+  using W = typename K::W;
+  extern __shared__ __align__(128) uint8_t raw[];
+  Smem<W>& s = *reinterpret_cast<Smem<W>*>(raw);
+  uint32_t* mask_s = reinterpret_cast<uint32_t*>(raw + smem_head<DT>());
+  T* slice = reinterpret_cast<T*>(raw + smem_head<DT>() + align_up(4 * size_t(p.slice_words), 128));
+  R r(p, s, mask_s, slice);
+
+  // 1. Start copying this rank's slice (and mask words) before waiting for
+  //    the preparation kernel: they are inputs, which it never writes.
+  if (threadIdx.x == 0) {
+    mbar_init(&s.bar, 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
+  const T* src = static_cast<const T*>(p.target) + int64_t(r.row) * p.t_s0;
+  const int n = r.hi - r.lo;
+  if (p.vector_load) {
+    const uint32_t bytes = uint32_t(n) * uint32_t(sizeof(T)), bulk = bytes & ~15u;
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(&s.bar, bulk);
+      const uint8_t* from = reinterpret_cast<const uint8_t*>(src + r.lo);
+      for (uint32_t off = 0; off < bulk; off += BULK_CHUNK)
+        bulk_load(reinterpret_cast<uint8_t*>(slice) + off, from + off, min(BULK_CHUNK, bulk - off), &s.bar);
+    }
+    for (int i = int(bulk / sizeof(T)) + threadIdx.x; i < n; i += THREADS) slice[i] = src[r.lo + i];
+  } else {
+    if (threadIdx.x == 0) mbar_arrive_expect_tx(&s.bar, 0);
+    for (int i = threadIdx.x; i < n; i += THREADS) slice[i] = src[int64_t(r.lo + i) * p.t_s1];
+  }
+  if (p.mask != nullptr)
+    for (int w = threadIdx.x; w < (n + 31) / 32; w += THREADS)
+      mask_s[w] = uint32_t(p.mask[int64_t(r.row) * p.m_s0 + int64_t(r.lo / 32 + w) * p.m_s1]);
+
+  // 2. The preparation kernel's statuses and counters, then the copy.
+  wait_for_prerequisite_grid();
+  bool lost = false;
+  for (uint32_t spins = 0; !mbar_try_wait(&s.bar, 0);)
+    if (++spins >= WAIT_LIMIT) {
+      lost = true;
+      break;
+    }
+  lost = __syncthreads_or(lost);
+  if (lost && threadIdx.x == 0) atomicAdd(&diagnostics(p.workspace, p.rows)->wait_timeouts, 1u);
+
+  // 3. The row's request and parameters (the same on every rank).
+  if (threadIdx.x == 0) {
+    RowCtx c{};
+    c.skip = *malformed_flag(p.workspace) != 0;
+    if (!c.skip) {
+      c.req = request_of(p, r.row);
+      c.skip = p.status[int64_t(c.req) * p.st_s] != ES_OK;
+    }
+    if (!c.skip) {
+      const int64_t q = c.req;
+      c.begin = int(at(p.cu_rows, p.cu_s, q));
+      c.end = int(at(p.cu_rows, p.cu_s, q + 1));
+      c.kind = int(at(p.draft_kind, p.kind_s, q));
+      c.draft_id = r.row + 1 < c.end ? int(p.draft_ids[q * p.d_s0 + int64_t(r.row - c.begin) * p.d_s1]) : -1;
+      c.temperature = at(p.temperature, p.temp_s, q);
+      c.top_p = at(p.top_p, p.topp_s, q);
+      c.min_p = at(p.min_p, p.minp_s, q);
+      c.top_k = at(p.top_k, p.topk_s, q);
+      c.seed = uint64_t(at(p.seeds, p.seed_s, q));
+      c.stream = uint32_t(at(p.streams, p.stream_s, q));
+      c.position = uint32_t(at(p.positions, p.pos_s, r.row));
+    }
+    s.ctx = c;
+  }
+  __syncthreads();
+  if (s.ctx.skip) return;  // the same decision on every rank; no rank reads another's memory
+  const RowCtx c = s.ctx;
+  const bool draft_row = r.row + 1 < c.end, full_q = draft_row && c.kind == 1;
+  const bool verify = draft_row && p.mode == ES_RATIO;
+  r.temperature = c.temperature;
+  r.top_p = c.top_p;
+  r.min_p = c.min_p;
+  r.addr = Address{c.stream, c.position, uint32_t(c.seed), uint32_t(c.seed >> 32)};
+
+  // 4. Validation and the row maximum.
+  r.stats_pass(full_q, lost);
+  RowResult res{ES_OK, ES_OK, 0, -1, -1, {0, 0, 0}};
+  res.target_status = r.all.bad ? ES_INVALID_INPUT : r.all.valid == 0 ? ES_NO_VALID_TOKEN : ES_OK;
+  res.status = res.target_status;
+  double sq = 0;
+  if (res.status == ES_OK && full_q) {
+    if (r.all.qbad) res.status = ES_INVALID_INPUT;
+    else if (r.all.qvalid == 0) res.status = ES_NO_VALID_TOKEN;
+    else {
+      sq = r.q_mass();
+      const W y = r.q_value(c.draft_id);
+      const double wq = y > W(-INFINITY) ? exp(double(y) - double(r.all.qmax)) : 0.0;
+      if (!(wq / sq > 0)) res.status = ES_DRAFT_ZERO_PROB;
+    }
+  }
+
+  // 5. The kept set, the ratio test and the draws.
+  if (res.status == ES_OK) {
+    if (c.temperature == 0) {
+      K::greedy(r, c, verify, full_q, sq, res);
+    } else {
+      const double inv = 1.0 / c.temperature;
+      r.slow_x = !(inv < 1e30 && inv > 1e-30);
+      r.inv_t = r.slow_x ? 0.f : float(inv);
+      r.ln_mp = c.min_p > 0 ? float(log(c.min_p)) : -INFINITY;
+      r.mp_tol = c.min_p > 0 ? 1e-6f * (1.f + fabsf(r.ln_mp)) : 0.f;
+      K::positive(r, c, verify, full_q, sq, res, p);
+    }
+  }
+
+  // 6. Publish; the request's last row to finish commits it.
+  r.cluster.sync();  // no rank reads another's shared memory after this point
+  if (r.rank == 0 && threadIdx.x == 0) {
+    row_results(p.workspace)[r.row] = res;
+    __threadfence();
+    const uint32_t done = atomicAdd(&arrivals(p.workspace, p.rows)[c.begin], 1u) + 1;
+    if (done == uint32_t(c.end - c.begin)) {
+      __threadfence();
+      finish_request(p, c.req, c.begin, c.end);
+    }
+  }
+}
+
+// Launch of the row kernel: a (C, rows) grid of C-block clusters, with
+// programmatic stream serialization after the preparation kernel.
+template <int DT> cudaError_t launch_rows(const Params& p, int cluster, cudaStream_t stream) {
+  const size_t smem = smem_bytes<DT>(p.slice_words);
+  auto kernel = rows_kernel<DT>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  if (cluster > 8) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(unsigned(cluster), unsigned(p.rows), 1);
+  config.blockDim = dim3(THREADS, 1, 1);
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = unsigned(cluster);
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attrs;
+  config.numAttrs = 2;
+  return cudaLaunchKernelEx(&config, kernel, p);
+}
+
+}  // namespace es

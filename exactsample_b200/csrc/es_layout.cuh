@@ -1,0 +1,96 @@
+// Kernel arguments, workspace layout and per-row records shared by the
+// preparation kernel, the row kernel and the host launcher.
+#pragma once
+#include "es_device.cuh"
+
+namespace es {
+
+constexpr int LIST_MAX = 256;   // largest kept set finished as an FP64 list (the plan's list_max caps it)
+constexpr int CAP = 1024;       // candidate buffer of a list row (cluster rank 0's shared memory)
+constexpr int DIST_BINS = 128;  // distance-below-maximum bins of 0.5 logit, plus one "far" bin
+constexpr int RADIX = 256;      // digits per radix-select level
+
+// Kernel arguments (filled by es_verify from es_args); strides in elements.
+struct Params {
+  const void* target;
+  int64_t t_s0, t_s1;
+  const void* draft;
+  int64_t q_s0, q_s1;
+  const int64_t* cu_rows;
+  int64_t cu_s;
+  const int64_t* draft_ids;
+  int64_t d_s0, d_s1;
+  const double* temperature;
+  int64_t temp_s;
+  const int64_t* top_k;
+  int64_t topk_s;
+  const double* top_p;
+  int64_t topp_s;
+  const double* min_p;
+  int64_t minp_s;
+  const int64_t* draft_kind;
+  int64_t kind_s;
+  const int64_t* seeds;
+  int64_t seed_s;
+  const int64_t* streams;
+  int64_t stream_s;
+  const int64_t* positions;
+  int64_t pos_s;
+  const int32_t* mask;
+  int64_t m_s0, m_s1;
+  uint8_t* workspace;
+  int64_t* tokens;
+  int64_t tok_s0, tok_s1;
+  int32_t* accepted;
+  int64_t acc_s;
+  int32_t* status;
+  int64_t st_s;
+  int32_t* path;
+  int64_t path_s;
+  int32_t rows, requests, vocab, max_draft;
+  int32_t mode, dispatch, list_max;
+  int32_t slice_words;     // 32-token mask words per cluster rank
+  int32_t vector_load;     // rows contiguous and 16-byte aligned: TMA bulk loads
+  int32_t offsets_inline;  // the preparation kernel validates cu_rows itself
+  int32_t exact_draws;     // dispatch="reference": every draw scored in FP64, no lists
+};
+
+// Per-row outcome, written by the row's cluster rank 0 and read by whichever
+// row of the request finishes last.
+struct RowResult {
+  int32_t target_status;  // status of the target distribution
+  int32_t status;         // target status, else the proposal's
+  int32_t accept;         // ratio mode: the draft was accepted
+  int32_t sample;         // substream-0 draw (bonus rows, coupled mode)
+  int32_t residual;       // substream-2 draw after a rejection (-1: no residual mass)
+  int32_t pad[3];
+};
+static_assert(sizeof(RowResult) == 32, "RowResult is 32 bytes");
+
+// Counters kept after the per-row arrays (reset by the preparation kernel).
+struct Diagnostics {
+  uint32_t near_ties;      // exact sums whose rounding sat within the fixed-point slack of a tie
+  uint32_t wait_timeouts;  // bounded waits that gave up
+  uint32_t pad[14];
+};
+
+// Workspace (bytes): [0] malformed-offsets flag, [4] FP64 recomputation count,
+// [8] RowResult[rows], then one arrival counter per row (used at each
+// request's first row), then Diagnostics. Always within the reference's
+// 8 + rows * (32 + 12288) bytes.
+__host__ __device__ inline int32_t* malformed_flag(uint8_t* ws) { return reinterpret_cast<int32_t*>(ws); }
+__host__ __device__ inline uint32_t* fallback_count(uint8_t* ws) { return reinterpret_cast<uint32_t*>(ws + 4); }
+__host__ __device__ inline RowResult* row_results(uint8_t* ws) { return reinterpret_cast<RowResult*>(ws + 8); }
+__host__ __device__ inline uint32_t* arrivals(uint8_t* ws, int64_t rows) {
+  return reinterpret_cast<uint32_t*>(ws + 8 + rows * sizeof(RowResult));
+}
+__host__ __device__ inline Diagnostics* diagnostics(uint8_t* ws, int64_t rows) {
+  return reinterpret_cast<Diagnostics*>(ws + 8 + rows * (sizeof(RowResult) + 4));
+}
+__host__ __device__ inline uint64_t workspace_needed(int64_t rows) {
+  return rows == 0 ? 8 : uint64_t(8 + rows * (sizeof(RowResult) + 4) + sizeof(Diagnostics));
+}
+
+template <class T> __device__ __forceinline__ T at(const T* p, int64_t stride, int64_t i) { return p[i * stride]; }
+
+}  // namespace es

@@ -1,0 +1,904 @@
+// The row kernel: one thread-block cluster per target row.
+//
+// Each of the cluster's C blocks ("ranks") owns a contiguous slice of the
+// row (a multiple of 32 tokens, so slices align with mask words and with the
+// Philox groups of four) and copies it once from HBM into its shared memory
+// with TMA bulk copies. Every later pass over the row (statistics, windows,
+// selections, sums, draws, FP64 rescoring) reads shared memory, and the ranks
+// combine partial results through distributed shared memory after a cluster
+// barrier. Each rank merges the C partial results itself, in rank order, so
+// every rank holds bitwise the same row-level values and takes the same
+// branches; no result depends on C, on the batch, or on timing.
+//
+// What a row computes follows the oracle (python/exactsample/reference.py,
+// distribution() and verify_reference()):
+//   validation and maximum          reference row_stats (csrc/verify/fused.cuh:409-519)
+//   top-k candidates near the max   row_hist / row_gather (fused.cuh:686-798)
+//   exact top-k cut                 buffer_select / select_next (fused.cuh:962-1184)
+//   FP64 list finish                fused_rows<LIST> (fused.cuh:1250-1444)
+//   full-row kept set and draws     fused_rows<FULL> (fused.cuh:1446-1785)
+//   ratio / coupled verification    fused.cuh:1396-1443, 1606-1621; verify.cu:169-217
+// Every decision is exact:
+//   * the kept set (mask, min-p, top-k, top-p): top-k by integer radix
+//     selection on order-preserving keys with token-ID tie breaking; min-p per
+//     token (FP32 with a margin, FP64 near the threshold); top-p by a radix
+//     selection weighted by FP64 weights summed exactly in 128-bit fixed
+//     point, i.e. the oracle's correctly rounded math.fsum;
+//   * normalizers and the ratio test: FP64 on exact sums, as in the oracle;
+//   * draws over lists (at most 256 tokens): the oracle's FP64 log(p) + G;
+//     over larger kept sets: a certified FP32 argmax of x + G with an FP64
+//     rescore of every token that could still win.
+#pragma once
+#include "es_prepare.cuh"
+
+namespace es {
+
+template <int DT> struct Types;
+template <> struct Types<ES_F32> { using T = float; using W = float; using Key = uint32_t; };
+template <> struct Types<ES_F64> { using T = double; using W = double; using Key = uint64_t; };
+template <> struct Types<ES_F16> { using T = __half; using W = float; using Key = uint32_t; };
+template <> struct Types<ES_BF16> { using T = __nv_bfloat16; using W = float; using Key = uint32_t; };
+
+__device__ __forceinline__ float widen(float v) { return v; }
+__device__ __forceinline__ double widen(double v) { return v; }
+__device__ __forceinline__ float widen(__half v) { return __half2float(v); }
+__device__ __forceinline__ float widen(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// Four consecutive values of a shared-memory slice.
+__device__ __forceinline__ void load4(const float* s, float v[4]) {
+  const float4 x = *reinterpret_cast<const float4*>(s);
+  v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+}
+__device__ __forceinline__ void load4(const double* s, double v[4]) {
+  const double2 x = reinterpret_cast<const double2*>(s)[0], y = reinterpret_cast<const double2*>(s)[1];
+  v[0] = x.x; v[1] = x.y; v[2] = y.x; v[3] = y.y;
+}
+__device__ __forceinline__ void load4(const __nv_bfloat16* s, float v[4]) {
+  const uint2 x = *reinterpret_cast<const uint2*>(s);
+  v[0] = __uint_as_float(x.x << 16); v[1] = __uint_as_float(x.x & 0xffff0000u);
+  v[2] = __uint_as_float(x.y << 16); v[3] = __uint_as_float(x.y & 0xffff0000u);
+}
+__device__ __forceinline__ void load4(const __half* s, float v[4]) {
+  const uint2 x = *reinterpret_cast<const uint2*>(s);
+  v[0] = __half2float(__ushort_as_half(uint16_t(x.x))); v[1] = __half2float(__ushort_as_half(uint16_t(x.x >> 16)));
+  v[2] = __half2float(__ushort_as_half(uint16_t(x.y))); v[3] = __half2float(__ushort_as_half(uint16_t(x.y >> 16)));
+}
+
+// An exact cut of the order (value desc, token ID asc): keeps the tokens at or
+// before (key, id). `on == 0` keeps everything.
+template <class Key> struct Cut {
+  int on;
+  Key key;
+  int id;
+  __device__ __forceinline__ bool keeps(Key k, int t) const { return !on || k > key || (k == key && t <= id); }
+};
+
+// |x32 - x| <= X_ERR |x| for x = (v - max) / T (three FP32 roundings, or one
+// FP64 -> FP32 conversion).
+constexpr float X_ERR = 2.0e-7f;
+// |s32 - (x + G)| <= SCORE_ERR (1 + |x32| + |G32|) for s32 = x32 + noise32:
+// X_ERR |x| + NOISE_ERR (1 + |G|) + one rounding of the sum, with margin.
+constexpr float SCORE_ERR = 1.5e-6f;
+// Tokens are pruned only this far below the best lower bound so far, so a
+// pruned bound rarely blocks the certificate of a different winner.
+constexpr float PRUNE_MARGIN = 1e-3f;
+// Distance windows (logits below the maximum) tried for list candidates.
+constexpr int WINDOWS = 8;
+__device__ __forceinline__ float window_width(int i) { return 0.25f * float(1 << i); }  // 0.25 .. 32
+
+// exp((v - max) / T) >= min_p and > 0 in FP64, for the rare token whose
+// FP32 value is too close to a threshold (out of line: keeps the loops lean).
+static __device__ __noinline__ bool weight_kept_fp64(double v, double maxv, double temperature, double min_p) {
+  const double w = exp((v - maxv) / temperature);
+  return w >= min_p && w > 0;
+}
+
+template <class W> struct Stats {
+  W b1v, b2v, qmax;
+  int32_t b1i, b2i, valid, bad, qvalid, qbad;
+};
+
+struct RowCtx {
+  int32_t req, begin, end, draft_id, kind, skip;
+  double temperature, top_p, min_p;
+  int64_t top_k;
+  uint64_t seed;
+  uint32_t stream, position;
+};
+
+template <class W> struct Smem {
+  uint64_t bar;
+  int32_t timeout;
+  RowCtx ctx;
+  // Published to the other ranks, double-buffered by exchange parity.
+  Stats<W> stats[2];
+  uint32_t hist[2][RADIX];
+  int32_t wcount[2][WINDOWS];
+  u128 fx[2];
+  uint32_t fxn[2];
+  Pick pick[2];
+  Best best[2];
+  int32_t slot[2];
+  // Block scratch.
+  union {
+    Pick picks[WARPS];
+    Best bests[WARPS];
+    u128 fxs[WARPS];
+    int32_t ints[WARPS];
+    uint32_t uints[WARPS];
+    int32_t win[WARPS][WINDOWS];
+    Stats<W> stats[WARPS];
+  } red;
+  int32_t ival[4];
+  u128 fxval;
+  double dval;
+  float floor_score;
+  int32_t n_cand;
+  // Rank 0's candidate buffer (list rows) or the weighted-selection buckets (top-p rows).
+  union {
+    struct {
+      uint64_t key[CAP];
+      int32_t id[CAP];
+    } cand;
+    u128 mass[2][RADIX];
+  } u;
+  // Rank 0's FP64 list: weights and probabilities in list order.
+  double lw[LIST_MAX];
+  double lp[LIST_MAX];
+};
+
+// Adds (v, 1) to bucket b of mass/count, aggregated over the warp's lanes that
+// share a bucket (one atomic per distinct bucket). Called by the whole warp;
+// lanes with b < 0 contribute nothing.
+__device__ __forceinline__ void warp_bucket_add(u128* mass, uint32_t* count, int b, u128 v) {
+  unsigned todo = __ballot_sync(0xffffffffu, b >= 0);
+  while (todo) {
+    const int leader = __ffs(todo) - 1;
+    const int bb = __shfl_sync(0xffffffffu, b, leader);
+    const unsigned same = __ballot_sync(0xffffffffu, b == bb);
+    u128 part = b == bb ? v : u128(0);
+    if (mass) part = warp_all(part, [](u128 a, u128 c) { return a + c; });
+    if (lane_id() == leader) {
+      if (mass) {
+        unsigned long long* m = reinterpret_cast<unsigned long long*>(&mass[bb]);
+        const unsigned long long lo = uint64_t(part), hi = uint64_t(part >> 64);
+        const unsigned long long old = atomicAdd(m, lo);
+        const unsigned long long carry = old + lo < old ? 1ull : 0ull;
+        if (hi + carry) atomicAdd(m + 1, hi + carry);
+      }
+      atomicAdd(&count[bb], uint32_t(__popc(same)));
+    }
+    todo &= ~same;
+  }
+}
+
+template <int DT> struct Row {
+  using T = typename Types<DT>::T;
+  using W = typename Types<DT>::W;
+  using Key = typename Types<DT>::Key;
+  static constexpr int KEY_BITS = int(sizeof(Key) * 8);
+
+  const Params& p;
+  Smem<W>& s;
+  uint32_t* mask_s;  // this rank's mask words
+  T* slice;          // this rank's logits
+  cg::cluster_group cluster;
+  int rank, ranks, row, lo, hi, groups;
+  int xc;  // exchanges so far (the same on every rank)
+
+  // Row-level values, identical on every rank after the statistics merge.
+  Stats<W> all;
+  W maxv;
+  double temperature, top_p, min_p;
+  float inv_t, ln_mp, mp_tol;
+  bool slow_x, has_mask;
+  Address addr;
+
+  __device__ Row(const Params& p_, Smem<W>& s_, uint32_t* m, T* sl)
+      : p(p_), s(s_), mask_s(m), slice(sl), cluster(cg::this_cluster()) {
+    rank = int(cluster.block_rank());
+    ranks = int(cluster.num_blocks());
+    row = blockIdx.y;
+    lo = min(p.vocab, rank * p.slice_words * 32);
+    hi = min(p.vocab, lo + p.slice_words * 32);
+    groups = (hi - lo + 3) / 4;
+    xc = 0;
+    has_mask = p.mask != nullptr;
+  }
+
+  // ---- slice access ----
+  // Mask bits of local group g (tokens allowed and inside the slice).
+  __device__ __forceinline__ unsigned group_bits(int g) const {
+    const int t = 4 * g;
+    unsigned bits = has_mask ? (mask_s[t >> 5] >> (t & 31)) & 0xfu : 0xfu;
+    const int left = hi - lo - t;
+    if (left < 4) bits &= (1u << max(left, 0)) - 1u;
+    return bits;
+  }
+  // Values of local group g and the bits of its valid tokens (allowed, inside
+  // the slice, above -inf).
+  __device__ __forceinline__ unsigned group(int g, W v[4]) const {
+    load4(slice + 4 * g, v);
+    unsigned bits = group_bits(g);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (!(v[j] > W(-INFINITY))) bits &= ~(1u << j);
+    return bits;
+  }
+  // A single token anywhere in the row, from global memory.
+  __device__ __forceinline__ W value_global(int t) const {
+    return widen(static_cast<const T*>(p.target)[int64_t(row) * p.t_s0 + int64_t(t) * p.t_s1]);
+  }
+  __device__ __forceinline__ bool allowed_global(int t) const {
+    return !has_mask || ((uint32_t(p.mask[int64_t(row) * p.m_s0 + int64_t(t >> 5) * p.m_s1]) >> (t & 31)) & 1u);
+  }
+  __device__ __forceinline__ bool valid_global(int t) const {
+    return allowed_global(t) && value_global(t) > W(-INFINITY);
+  }
+  __device__ __forceinline__ W q_value(int t) const {
+    return widen(static_cast<const T*>(p.draft)[int64_t(row) * p.q_s0 + int64_t(t) * p.q_s1]);
+  }
+
+  // ---- cluster exchange ----
+  // Publish into slot parity(), exchange(), then read slot parity() ^ 1 of
+  // every rank. A slot is rewritten two exchanges later, after every rank has
+  // passed the exchange that follows its reads.
+  __device__ __forceinline__ int parity() const { return xc & 1; }
+  __device__ __forceinline__ void exchange() {
+    cluster.sync();
+    ++xc;
+  }
+  template <class X> __device__ __forceinline__ X* peer(X* local, int r) { return cluster.map_shared_rank(local, r); }
+
+  // ---- temperature-scaled values ----
+  __device__ __forceinline__ double x64(W v) const { return (double(v) - double(maxv)) / temperature; }
+  __device__ __forceinline__ float x32(W v) const {
+    if constexpr (sizeof(W) == 8) {
+      return __double2float_rn(x64(v));
+    } else {
+      if (slow_x) return __double2float_rn(x64(v));
+      return __fmul_rn(__fsub_rn(v, maxv), inv_t);
+    }
+  }
+  // w = exp(x64) >= min_p and w > 0, decided exactly: FP32 settles tokens
+  // clear of both thresholds, FP64 the rest.
+  __device__ __forceinline__ bool weight_kept(W v, float x) const {
+    const float tol = __fadd_rn(__fmul_rn(X_ERR, fabsf(x)), mp_tol);
+    const float gap = __fsub_rn(x, ln_mp);
+    if (x > -744.f && gap > tol) return true;
+    if (x < -746.f || gap < -tol) return false;
+    return weight_kept_fp64(double(v), double(maxv), temperature, min_p);
+  }
+  __device__ __forceinline__ bool exact_weight_kept(W v) const {
+    return weight_kept_fp64(double(v), double(maxv), temperature, min_p);
+  }
+
+  __device__ void count_fallback() {
+    if (rank == 0 && threadIdx.x == 0) atomicAdd(fallback_count(p.workspace), 1u);
+  }
+  __device__ void count_near_tie(bool near) {
+    if (near && rank == 0 && threadIdx.x == 0) atomicAdd(&diagnostics(p.workspace, p.rows)->near_ties, 1u);
+  }
+
+  // ---- the statistics pass ----
+  __device__ static Stats<W> merge_stats(Stats<W> a, Stats<W> b) {
+    auto better = [](W av, int ai, W bv, int bi) { return av > bv || (av == bv && ai < bi); };
+    const bool b_first = better(b.b1v, b.b1i, a.b1v, a.b1i);
+    const W w1 = b_first ? b.b1v : a.b1v, l1 = b_first ? a.b1v : b.b1v, w2 = b_first ? b.b2v : a.b2v;
+    const int w1i = b_first ? b.b1i : a.b1i, l1i = b_first ? a.b1i : b.b1i, w2i = b_first ? b.b2i : a.b2i;
+    Stats<W> r;
+    r.b1v = w1;
+    r.b1i = w1i;
+    const bool l_second = better(l1, l1i, w2, w2i);
+    r.b2v = l_second ? l1 : w2;
+    r.b2i = l_second ? l1i : w2i;
+    r.qmax = a.qmax > b.qmax ? a.qmax : b.qmax;
+    r.valid = a.valid + b.valid;
+    r.bad = a.bad | b.bad;
+    r.qvalid = a.qvalid + b.qvalid;
+    r.qbad = a.qbad | b.qbad;
+    return r;
+  }
+  __device__ Stats<W> block_stats(Stats<W> v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      Stats<W> y;
+      y.b1v = shfl_xor(v.b1v, o); y.b2v = shfl_xor(v.b2v, o); y.qmax = shfl_xor(v.qmax, o);
+      y.b1i = shfl_xor(v.b1i, o); y.b2i = shfl_xor(v.b2i, o); y.valid = shfl_xor(v.valid, o);
+      y.bad = shfl_xor(v.bad, o); y.qvalid = shfl_xor(v.qvalid, o); y.qbad = shfl_xor(v.qbad, o);
+      v = merge_stats(v, y);
+    }
+    if (lane_id() == 0) s.red.stats[warp_id()] = v;
+    __syncthreads();
+    Stats<W> r = s.red.stats[0];
+    for (int w = 1; w < WARPS; ++w) r = merge_stats(r, s.red.stats[w]);
+    __syncthreads();
+    return r;
+  }
+  // NaN / +inf anywhere (even masked), the count of valid tokens, the
+  // maximum with the lowest ID among equals, the runner-up, and for a full-q
+  // draft row the same checks of the proposal row.
+  __device__ void stats_pass(bool full_q, bool timed_out) {
+    W b1v = W(-INFINITY), b2v = W(-INFINITY), qmax = W(-INFINITY);
+    int b1i = INT_MAX, b2i = INT_MAX, nvalid = 0, bad = 0, qvalid = 0, qbad = 0;
+    for (int g = threadIdx.x; g < groups; g += THREADS) {
+      W v[4];
+      load4(slice + 4 * g, v);
+      const unsigned bits = group_bits(g);
+      const int inside = min(4, hi - lo - 4 * g);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (j >= inside) break;
+        bad |= isnan(v[j]) | (v[j] == W(INFINITY));
+        const bool ok = ((bits >> j) & 1u) && v[j] > W(-INFINITY);
+        nvalid += ok;
+        const int t = lo + 4 * g + j;
+        if (ok && v[j] > b1v) {  // IDs rise within a thread, so ties keep the lowest
+          b2v = b1v; b2i = b1i; b1v = v[j]; b1i = t;
+        } else if (ok && v[j] > b2v) {
+          b2v = v[j]; b2i = t;
+        }
+      }
+    }
+    if (full_q)
+      for (int t = lo + int(threadIdx.x); t < hi; t += THREADS) {
+        const W y = q_value(t);
+        qbad |= isnan(y) | (y == W(INFINITY));
+        qvalid += y > W(-INFINITY);
+        qmax = y > qmax ? y : qmax;
+      }
+    if (timed_out) bad = 1;  // this rank's slice never arrived: the row is not trusted
+    const Stats<W> merged = block_stats(Stats<W>{b1v, b2v, qmax, b1i, b2i, nvalid, bad, qvalid, qbad});
+    if (threadIdx.x == 0) s.stats[parity()] = merged;
+    exchange();
+    all = *peer(&s.stats[parity() ^ 1], 0);
+    for (int r = 1; r < ranks; ++r) all = merge_stats(all, *peer(&s.stats[parity() ^ 1], r));
+    maxv = all.b1v;
+  }
+
+  // ---- cluster-wide reductions ----
+  __device__ u128 cluster_sum(u128 local, uint32_t n_local, uint32_t* n_total) {
+    const u128 bsum = block_all(local, [](u128 a, u128 b) { return a + b; }, s.red.fxs);
+    const uint32_t bn = block_all(n_local, [](uint32_t a, uint32_t b) { return a + b; }, s.red.uints);
+    if (threadIdx.x == 0) {
+      s.fx[parity()] = bsum;
+      s.fxn[parity()] = bn;
+    }
+    exchange();
+    u128 total = 0;
+    uint32_t n = 0;
+    for (int r = 0; r < ranks; ++r) {
+      total += *peer(&s.fx[parity() ^ 1], r);
+      n += *peer(&s.fxn[parity() ^ 1], r);
+    }
+    *n_total = n;
+    return total;
+  }
+  __device__ int cluster_min(int local) {
+    const int b = block_all(local, [](int a, int c) { return a < c ? a : c; }, s.red.ints);
+    if (threadIdx.x == 0) s.slot[parity()] = b;
+    exchange();
+    int m = INT_MAX;
+    for (int r = 0; r < ranks; ++r) m = min(m, *peer(&s.slot[parity() ^ 1], r));
+    return m;
+  }
+
+  // ---- radix selection (integer, exact) ----
+  // The n-th (1-based) valid token in (value desc, ID asc) order among those
+  // `admit` accepts (1 <= n <= their count): 8-bit digits of the order key
+  // from the top, one shared-memory pass and one cluster exchange of 256
+  // counts per level, then the n-th lowest ID among tokens with that key.
+  template <class Admit> __device__ Cut<Key> select_nth(int n, Admit admit) {
+    Key prefix = 0, known = 0;
+    int need = n, digit = 0;
+    for (int shift = KEY_BITS - 8; shift >= 0; shift -= 8) {
+      uint32_t* h = s.hist[parity()];
+      for (int i = threadIdx.x; i < RADIX; i += THREADS) h[i] = 0;
+      __syncthreads();
+      for (int base = warp_id() * 32; base < groups; base += THREADS) {
+        const int g = base + lane_id();
+        W v[4];
+        unsigned bits = 0;
+        if (g < groups) bits = group(g, v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          int d = -1;
+          if ((bits >> j) & 1u) {
+            const Key k = order_key(v[j]);
+            if ((k & known) == prefix && admit(k, lo + 4 * g + j, v[j])) d = int((k >> shift) & 255);
+          }
+          warp_bucket_add(nullptr, h, d, 0);
+        }
+      }
+      exchange();
+      // Thread i owns digit 255 - i: merged counts, scanned from the top.
+      int cnt = 0;
+      for (int r = 0; r < ranks; ++r) cnt += int(peer(s.hist[parity() ^ 1], r)[255 - threadIdx.x]);
+      int total;
+      const int cum = block_scan(cnt, s.red.ints, &total);
+      if (cum >= need && cum - cnt < need) {
+        s.ival[0] = 255 - int(threadIdx.x);
+        s.ival[1] = cum - cnt;
+      }
+      __syncthreads();
+      digit = s.ival[0];
+      need -= s.ival[1];
+      prefix |= Key(digit) << shift;
+      known |= Key(255) << shift;
+      __syncthreads();
+    }
+    // Ties at the key: ranks own contiguous ID ranges, so the last level's
+    // per-rank counts of the digit locate the need-th lowest ID.
+    int before = 0, owner = -1;
+    for (int r = 0; r < ranks && owner < 0; ++r) {
+      const int c = int(peer(s.hist[parity() ^ 1], r)[digit]);
+      if (before + c >= need) owner = r;
+      else before += c;
+    }
+    int id = INT_MAX;
+    if (owner == rank)
+      id = nth_local(need - before, [&](W v, int t, Key k) { return k == prefix && admit(k, t, v); });
+    id = cluster_min(owner == rank ? id : INT_MAX);
+    return Cut<Key>{1, prefix, id};
+  }
+
+  // The n-th (1-based) valid token of this rank's slice in ID order that
+  // `match` accepts; INT_MAX if there are fewer. Block-uniform.
+  template <class Match> __device__ int nth_local(int n, Match match) {
+    const int per = (groups + THREADS - 1) / THREADS;  // thread i takes groups [i*per, (i+1)*per)
+    const int g0 = threadIdx.x * per, g1 = min(groups, g0 + per);
+    int c = 0;
+    for (int g = g0; g < g1; ++g) {
+      W v[4];
+      const unsigned bits = group(g, v);
+      for (int j = 0; j < 4; ++j) c += ((bits >> j) & 1u) && match(v[j], lo + 4 * g + j, order_key(v[j]));
+    }
+    int total;
+    const int incl = block_scan(c, s.red.ints, &total);
+    int found = INT_MAX;
+    if (incl >= n && incl - c < n) {
+      int k = incl - c;
+      for (int g = g0; g < g1 && found == INT_MAX; ++g) {
+        W v[4];
+        const unsigned bits = group(g, v);
+        for (int j = 0; j < 4; ++j)
+          if (((bits >> j) & 1u) && match(v[j], lo + 4 * g + j, order_key(v[j])) && ++k == n) {
+            found = lo + 4 * g + j;
+            break;
+          }
+      }
+    }
+    return block_all(found, [](int a, int b) { return a < b ? a : b; }, s.red.ints);
+  }
+
+  // ---- list candidates ----
+  // Appends this rank's valid tokens that `take` accepts to rank 0's
+  // candidate buffer from `offset` on (there are at most CAP in all), then
+  // exchanges.
+  template <class Take> __device__ void gather(int offset, Take take) {
+    if (threadIdx.x == 0) s.n_cand = 0;
+    __syncthreads();
+    uint64_t* keys = peer(s.u.cand.key, 0);
+    int32_t* ids = peer(s.u.cand.id, 0);
+    for (int g = threadIdx.x; g < groups; g += THREADS) {
+      W v[4];
+      const unsigned bits = group(g, v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int t = lo + 4 * g + j;
+        if (!((bits >> j) & 1u) || !take(v[j], t)) continue;
+        const int at_ = offset + atomicAdd(&s.n_cand, 1);
+        if (at_ < CAP) {
+          keys[at_] = uint64_t(order_key(v[j]));
+          ids[at_] = t;
+        }
+      }
+    }
+    exchange();
+  }
+  // Counts this rank's valid tokens that `take` accepts, exchanges, and
+  // gathers them to rank 0 if they fit; returns the total (> CAP: nothing
+  // was gathered).
+  template <class Take> __device__ int gather_all(Take take) {
+    int c = 0;
+    for (int g = threadIdx.x; g < groups; g += THREADS) {
+      W v[4];
+      const unsigned bits = group(g, v);
+      for (int j = 0; j < 4; ++j) c += ((bits >> j) & 1u) && take(v[j], lo + 4 * g + j);
+    }
+    c = block_all(c, [](int a, int b) { return a + b; }, s.red.ints);
+    if (threadIdx.x == 0) s.slot[parity()] = c;
+    exchange();
+    int total = 0, offset = 0;
+    for (int r = 0; r < ranks; ++r) {
+      const int cr = *peer(&s.slot[parity() ^ 1], r);
+      total += cr;
+      if (r < rank) offset += cr;
+    }
+    if (total <= CAP) gather(offset, take);
+    return total;
+  }
+  // The top-n valid tokens (and ties at the n-th value) near the maximum:
+  // the narrowest distance window below the maximum that holds at least n
+  // tokens and at most CAP is gathered to rank 0. Returns the count, or -1
+  // if no window qualifies.
+  __device__ int gather_window(int n) {
+    int c[WINDOWS] = {};
+    for (int g = threadIdx.x; g < groups; g += THREADS) {
+      W v[4];
+      const unsigned bits = group(g, v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (!((bits >> j) & 1u)) continue;
+        const float d = float(maxv - v[j]);  // monotone in v
+#pragma unroll
+        for (int i = 0; i < WINDOWS; ++i) c[i] += d <= window_width(i);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < WINDOWS; ++i) c[i] = warp_all(c[i], [](int a, int b) { return a + b; });
+    if (lane_id() == 0)
+      for (int i = 0; i < WINDOWS; ++i) s.red.win[warp_id()][i] = c[i];
+    __syncthreads();
+    if (threadIdx.x < WINDOWS) {
+      int t = 0;
+      for (int w = 0; w < WARPS; ++w) t += s.red.win[w][threadIdx.x];
+      s.wcount[parity()][threadIdx.x] = t;
+    }
+    exchange();
+    int pick = -1, total = 0, offset = 0;
+    for (int i = 0; i < WINDOWS && pick < 0; ++i) {
+      int t = 0, before = 0;
+      for (int r = 0; r < ranks; ++r) {
+        const int cr = peer(s.wcount[parity() ^ 1], r)[i];
+        t += cr;
+        if (r < rank) before += cr;
+      }
+      if (t >= n && t <= CAP) { pick = i; total = t; offset = before; }
+    }
+    if (pick < 0) return -1;
+    const float width = window_width(pick);
+    gather(offset, [&](W v, int) { return float(maxv - v) <= width; });
+    return total;
+  }
+
+  // Sorts rank 0's m candidates into (key desc, ID asc) order (bitonic).
+  __device__ void sort_candidates(int m) {
+    int size = 1;
+    while (size < m) size <<= 1;
+    uint64_t* key = s.u.cand.key;
+    int32_t* id = s.u.cand.id;
+    for (int i = m + threadIdx.x; i < size; i += THREADS) {
+      key[i] = 0;
+      id[i] = INT_MAX;
+    }
+    __syncthreads();
+    for (int k = 2; k <= size; k <<= 1)
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = threadIdx.x; i < size; i += THREADS) {
+          const int l = i ^ j;
+          if (l <= i) continue;
+          const bool desc = (i & k) == 0;
+          const bool i_first = key[i] > key[l] || (key[i] == key[l] && id[i] < id[l]);
+          if (i_first != desc) {
+            const uint64_t tk = key[i]; key[i] = key[l]; key[l] = tk;
+            const int32_t ti = id[i]; id[i] = id[l]; id[l] = ti;
+          }
+        }
+        __syncthreads();
+      }
+  }
+
+  // ---- exact sums ----
+  // Sum of exact FP64 weights over this row's valid tokens that `kept`
+  // accepts (with the exact min-p test), over the cluster.
+  template <class Kept> __device__ double exact_mass(Kept kept) {
+    u128 acc = 0;
+    uint32_t n = 0;
+    for (int g = threadIdx.x; g < groups; g += THREADS) {
+      W v[4];
+      const unsigned bits = group(g, v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (!((bits >> j) & 1u) || !kept(order_key(v[j]), lo + 4 * g + j)) continue;
+        const double w = exp(x64(v[j]));
+        if (!(w >= min_p && w > 0)) continue;
+        acc += fx_of(w);
+        ++n;
+      }
+    }
+    uint32_t total_n;
+    const u128 total = cluster_sum(acc, n, &total_n);
+    bool near;
+    const double r = fx_round(total, total_n, &near);
+    count_near_tie(near);
+    return r;
+  }
+  // The proposal's normalizer: the exact sum of exp(y - max y) over the q row.
+  __device__ double q_mass() {
+    u128 acc = 0;
+    uint32_t n = 0;
+    for (int t = lo + int(threadIdx.x); t < hi; t += THREADS) {
+      const W y = q_value(t);
+      if (!(y > W(-INFINITY))) continue;
+      const double w = exp(double(y) - double(all.qmax));
+      if (!(w > 0)) continue;
+      acc += fx_of(w);
+      ++n;
+    }
+    uint32_t total_n;
+    const u128 total = cluster_sum(acc, n, &total_n);
+    bool near;
+    const double r = fx_round(total, total_n, &near);
+    count_near_tie(near);
+    return r;
+  }
+
+  // ---- top-p over a full row ----
+  // The shortest prefix of the kept set K (valid, cut_k, min-p) in (value
+  // desc, ID asc) order whose correctly rounded sum reaches top_p * fsum(K):
+  // a radix selection over the order key whose buckets carry exact weight
+  // sums, then the tie position inside the selected key. Returns the cut and
+  // the prefix's rounded sum (the normalizer).
+  __device__ Cut<Key> top_p_cut(Cut<Key> cut_k, double* normalizer) {
+    Key prefix = 0, known = 0;
+    u128 above = 0;
+    uint32_t above_n = 0;
+    double target = 0;
+    int digit = 0, last_count = 0;
+    for (int shift = KEY_BITS - 8; shift >= 0; shift -= 8) {
+      u128* mass = s.u.mass[parity()];
+      uint32_t* count = s.hist[parity()];
+      for (int i = threadIdx.x; i < RADIX; i += THREADS) {
+        mass[i] = 0;
+        count[i] = 0;
+      }
+      __syncthreads();
+      for (int base = warp_id() * 32; base < groups; base += THREADS) {
+        const int g = base + lane_id();
+        W v[4];
+        unsigned bits = 0;
+        if (g < groups) bits = group(g, v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          int d = -1;
+          u128 f = 0;
+          if ((bits >> j) & 1u) {
+            const Key k = order_key(v[j]);
+            const int t = lo + 4 * g + j;
+            if ((k & known) == prefix && cut_k.keeps(k, t)) {
+              const double w = exp(x64(v[j]));
+              if (w >= min_p && w > 0) {
+                d = int((k >> shift) & 255);
+                f = fx_of(w);
+              }
+            }
+          }
+          warp_bucket_add(mass, count, d, f);
+        }
+      }
+      exchange();
+      // Thread i owns digit 255 - i: merged mass and count, scanned from the top.
+      u128 m = 0;
+      uint32_t c = 0;
+      for (int r = 0; r < ranks; ++r) {
+        m += peer(s.u.mass[parity() ^ 1], r)[255 - threadIdx.x];
+        c += peer(s.hist[parity() ^ 1], r)[255 - threadIdx.x];
+      }
+      u128 m_total;
+      uint32_t c_total;
+      const u128 m_cum = block_scan(m, s.red.fxs, &m_total);
+      const uint32_t c_cum = block_scan(c, s.red.uints, &c_total);
+      if (shift == KEY_BITS - 8) {
+        bool near;
+        const double total = fx_round(m_total, c_total, &near);
+        count_near_tie(near);
+        target = top_p * total;
+        if (target <= 1.0) {
+          // The first kept token (the maximum, weight exactly 1) reaches it.
+          *normalizer = 1.0;
+          return Cut<Key>{1, order_key(maxv), all.b1i};
+        }
+      }
+      bool near = false;
+      const bool reach = c > 0 && fx_reaches(above + m_cum, above_n + c_cum, target, &near);
+      if (reach && near) atomicAdd(&diagnostics(p.workspace, p.rows)->near_ties, rank == 0 ? 1u : 0u);
+      int first = block_all(reach ? int(threadIdx.x) : INT_MAX, [](int a, int b) { return a < b ? a : b; },
+                            s.red.ints);
+      if (first == INT_MAX) first = 255 - last_nonempty();  // unreachable with exact sums; keep the last bucket
+      if (int(threadIdx.x) == first) {
+        s.fxval = m_cum - m;
+        s.ival[0] = 255 - first;
+        s.ival[1] = int(c_cum - c);
+        s.ival[2] = int(c);
+      }
+      __syncthreads();
+      above += s.fxval;
+      above_n += uint32_t(s.ival[1]);
+      digit = s.ival[0];
+      last_count = s.ival[2];
+      prefix |= Key(digit) << shift;
+      known |= Key(255) << shift;
+      __syncthreads();
+    }
+    // The selected key's tokens are tied, with one weight w*: the boundary is
+    // the j-th of them in ID order, j the smallest with fl(above + j w*) >= target.
+    const W v_star = key_value(prefix);
+    const u128 w_star = fx_of(exp(x64(v_star)));
+    int lo_j = 1, hi_j = last_count;
+    bool near = false;
+    while (lo_j < hi_j) {
+      const int mid = (lo_j + hi_j) / 2;
+      bool nr;
+      if (fx_reaches(above + w_star * u128(mid), above_n + mid, target, &nr)) hi_j = mid;
+      else lo_j = mid + 1;
+    }
+    const int j = max(lo_j, 1);
+    *normalizer = fx_round(above + w_star * u128(j), above_n + j, &near);
+    count_near_tie(near);
+    int before = 0, owner = -1;
+    for (int r = 0; r < ranks && owner < 0; ++r) {
+      const int c = int(peer(s.hist[parity() ^ 1], r)[digit]);
+      if (before + c >= j) owner = r;
+      else before += c;
+    }
+    int id = INT_MAX;
+    if (owner == rank)
+      id = nth_local(j - before, [&](W v, int t, Key k) {
+        return k == prefix && cut_k.keeps(k, t) && exact_weight_kept(v);
+      });
+    id = cluster_min(owner == rank ? id : INT_MAX);
+    return Cut<Key>{1, prefix, id};
+  }
+  __device__ int last_nonempty() { return 0; }
+
+  // ---- draws ----
+  // Certified FP32 argmax of x + G over the valid tokens that `kept` accepts
+  // (and min-p keeps), except `excluded`; an FP64 rescore of every token
+  // whose bound reaches the FP32 winner's lower bound when the certificate
+  // fails (or of every token, with exact_only). Returns -1 if none is kept.
+  template <class Kept> __device__ int draw(uint32_t sub, int excluded, Kept kept, bool exact_only) {
+    if (threadIdx.x == 0) {
+      // A kept token's score bounds the winner's from below: the maximum
+      // (x = 0), or the runner-up when the maximum is excluded.
+      float floor = -INFINITY;
+      const int t = all.b1i != excluded ? all.b1i : all.b2i;
+      if (t != INT_MAX && valid_global(t)) {
+        const W v = value_global(t);
+        const float x = x32(v);
+        if (kept(order_key(v), t) && weight_kept(v, x)) {
+          const float g = noise32(addr.word(sub, uint32_t(t)));
+          const float sc = __fadd_rn(x, g);
+          floor = __fsub_rn(sc, 1.01f * SCORE_ERR * (1.f + fabsf(x) + fabsf(g)));
+        }
+      }
+      s.floor_score = floor;
+    }
+    __syncthreads();
+    const float floor = exact_only ? -INFINITY : s.floor_score;
+    Pick best = no_pick();
+    float skipped = -INFINITY;
+    if (!exact_only) {
+      for (int g = threadIdx.x; g < groups; g += THREADS) {
+        W v[4];
+        const unsigned bits = group(g, v);
+        float xs[4];
+        unsigned live = 0;
+        const float bar = fmaxf(floor, best.lo) - PRUNE_MARGIN;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int t = lo + 4 * g + j;
+          xs[j] = 0.f;
+          if (!((bits >> j) & 1u) || t == excluded) continue;
+          const float x = x32(v[j]);
+          if (!kept(order_key(v[j]), t) || !weight_kept(v[j], x)) continue;
+          xs[j] = x;
+          const float ub = x + NOISE_MAX + SCORE_ERR * (1.f + fabsf(x) + NOISE_MAX);
+          if (ub >= bar) live |= 1u << j;
+          else skipped = fmaxf(skipped, ub);
+        }
+        if (!live) continue;
+        const Words r = addr.group(sub, uint32_t((lo >> 2) + g));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (!((live >> j) & 1u)) continue;
+          const float x = xs[j];
+          const float gu = noise_upper(r.w[j]);
+          const float ub = x + gu + SCORE_ERR * (1.f + fabsf(x) + fabsf(gu));
+          if (ub < fmaxf(floor, best.lo) - PRUNE_MARGIN) {
+            skipped = fmaxf(skipped, ub);
+            continue;
+          }
+          const float G = noise32(r.w[j]);
+          const float sc = __fadd_rn(x, G);
+          const float err = SCORE_ERR * (1.f + fabsf(x) + fabsf(G));
+          best = pick_of(best, Pick{sc, sc - err, sc + err, -INFINITY, lo + 4 * g + j});
+        }
+      }
+    }
+    best.others = fmaxf(best.others, skipped);
+    best = block_all(best, [](Pick a, Pick b) { return pick_of(a, b); }, s.red.picks);
+    if (threadIdx.x == 0) s.pick[parity()] = best;
+    exchange();
+    Pick top = no_pick();
+    for (int r = 0; r < ranks; ++r) top = pick_of(top, *peer(&s.pick[parity() ^ 1], r));
+    if (!exact_only) {
+      if (top.id == INT_MAX) return -1;
+      if (top.lo > top.others) return top.id;
+      count_fallback();
+    }
+    // FP64: every kept token whose upper bound reaches the threshold.
+    const float threshold = exact_only ? -INFINITY : top.lo;
+    Best b = no_best();
+    for (int g = threadIdx.x; g < groups; g += THREADS) {
+      W v[4];
+      const unsigned bits = group(g, v);
+      unsigned live = 0;
+      float xs[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int t = lo + 4 * g + j;
+        xs[j] = 0.f;
+        if (!((bits >> j) & 1u) || t == excluded) continue;
+        const float x = x32(v[j]);
+        if (!kept(order_key(v[j]), t) || !weight_kept(v[j], x)) continue;
+        xs[j] = x;
+        if (exact_only || x + NOISE_MAX + SCORE_ERR * (1.f + fabsf(x) + NOISE_MAX) >= threshold) live |= 1u << j;
+      }
+      if (!live) continue;
+      const Words r = addr.group(sub, uint32_t((lo >> 2) + g));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (!((live >> j) & 1u)) continue;
+        if (!exact_only) {
+          const float gu = noise_upper(r.w[j]);
+          if (xs[j] + gu + SCORE_ERR * (1.f + fabsf(xs[j]) + fabsf(gu)) < threshold) continue;
+        }
+        b = best_of(b, Best{x64(v[j]) + noise64(r.w[j]), lo + 4 * g + j});
+      }
+    }
+    b = block_all(b, [](Best a, Best c) { return best_of(a, c); }, s.red.bests);
+    if (threadIdx.x == 0) s.best[parity()] = b;
+    exchange();
+    Best winner = no_best();
+    for (int r = 0; r < ranks; ++r) winner = best_of(winner, *peer(&s.best[parity() ^ 1], r));
+    return winner.id == INT_MAX ? -1 : winner.id;
+  }
+
+  // The residual draw max(p - q, 0) of a full-q draft row over the kept set,
+  // in FP64 exactly as the oracle forms it: p = w / Sp, q = wq / Sq.
+  template <class Kept> __device__ int draw_residual_q(Kept kept, double sp, double sq) {
+    Best b = no_best();
+    for (int g = threadIdx.x; g < groups; g += THREADS) {
+      W v[4];
+      const unsigned bits = group(g, v);
+      bool any = false;
+      double r4[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        r4[j] = 0;
+        const int t = lo + 4 * g + j;
+        if (!((bits >> j) & 1u) || !kept(order_key(v[j]), t)) continue;
+        const double w = exp(x64(v[j]));
+        if (!(w >= min_p && w > 0)) continue;
+        const W y = q_value(t);
+        const double q = y > W(-INFINITY) ? exp(double(y) - double(all.qmax)) / sq : 0.0;
+        r4[j] = fmax(w / sp - q, 0.0);
+        any |= r4[j] > 0;
+      }
+      if (!any) continue;
+      const Words r = addr.group(2, uint32_t((lo >> 2) + g));
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (r4[j] > 0) b = best_of(b, Best{log(r4[j]) + noise64(r.w[j]), lo + 4 * g + j});
+    }
+    b = block_all(b, [](Best a, Best c) { return best_of(a, c); }, s.red.bests);
+    if (threadIdx.x == 0) s.best[parity()] = b;
+    exchange();
+    Best winner = no_best();
+    for (int r = 0; r < ranks; ++r) winner = best_of(winner, *peer(&s.best[parity() ^ 1], r));
+    return winner.id == INT_MAX ? -1 : winner.id;
+  }
+};
+
+}  // namespace es

@@ -1,0 +1,118 @@
+"""The drop-in Python API on the GPU: ownership, capacity, aliasing, strided
+outputs, malformed offsets and refusals, as the reference's
+tests/test_cuda.py:99-169 exercise them."""
+import numpy as np
+import pytest
+
+from exactsample_b200 import Status
+from tests import cases as C
+from tests.gpu_helpers import device_inputs, run_api
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    import torch
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+
+
+def prepared(rows, offsets, ids, strided=False, **kw):
+    """(verify keyword arguments, tensors) for a small case, like the reference's prepared_cuda."""
+    from exactsample_b200.cuda import CudaRequestParams, CudaRngKey, plan
+    case = C._case("api", np.asarray(rows, dtype=np.float64), offsets, C._drafts(ids, len(offsets) - 1), **kw)
+    t = device_inputs(case, strided=strided)
+    work = plan(case["logits"].shape[0], len(offsets) - 1, t["_max_draft"], case["logits"].shape[1], reference=True)
+    args = dict(target_logits=t["target_logits"], cu_rows=t["cu_rows"], draft_ids=t["draft_ids"],
+                params=CudaRequestParams(t["temperature"], t["top_k"], t["top_p"], t["min_p"], t["draft_kind"]),
+                rng=CudaRngKey(t["seeds"], t["stream_ids"], t["positions"]), plan=work, out=work.allocate_output())
+    return args
+
+
+def test_workspace_conflict_and_separate_plans():
+    import torch
+    from exactsample_b200.cuda import verify
+    args = prepared(np.zeros((1, 4)), [0, 1], np.empty((1, 0)))
+    other = prepared(np.zeros((1, 4)), [0, 1], np.empty((1, 0)))
+    first, second = torch.cuda.Stream(), torch.cuda.Stream()
+    first.wait_stream(torch.cuda.current_stream())
+    second.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(first):
+        torch.cuda._sleep(100_000_000)
+        verify(**args)
+    with torch.cuda.stream(second):
+        with pytest.raises(RuntimeError, match="in flight"):
+            verify(**args)
+        verify(**other)
+    args["plan"].synchronize()
+    other["plan"].synchronize()
+    assert args["out"].tokens.cpu().tolist() == other["out"].tokens.cpu().tolist()
+
+
+def test_capacity_and_large_k_on_fused_path():
+    import torch
+    from exactsample_b200.cuda import verify
+    case = C._case("k65", np.zeros((1, 100)), [0, 1], np.empty((1, 0), np.int64), top_k=65)
+    out, _ = run_api(case, dispatch="fused")
+    assert out.path_used.cpu().tolist() == [1]
+    args = prepared(np.zeros((1, 100)), [0, 1], np.empty((1, 0)))
+    args["target_logits"] = torch.zeros((2, 100), device="cuda")
+    with pytest.raises(ValueError, match="capacity"):
+        verify(**args)
+
+
+def test_output_alias_is_rejected():
+    from exactsample_b200.cuda import verify
+    args = prepared(np.zeros((1, 4)), [0, 1], np.empty((1, 0)))
+    args["out"].tokens = args["rng"].seed.reshape(1, 1)
+    with pytest.raises(RuntimeError, match="alias"):
+        verify(**args)
+
+
+def test_noncontiguous_outputs_keep_their_gaps():
+    import torch
+    from exactsample_b200.cuda import verify
+    args = prepared(np.zeros((3, 4)), [0, 1, 3], [[-1], [2]], strided=True)
+    out = args["out"]
+    backing = torch.full((2, 4), -777, dtype=torch.int64, device="cuda")
+    out.tokens = backing[:, ::2]
+    for field in ["accepted_len", "status", "path_used"]:
+        setattr(out, field, torch.empty(4, dtype=torch.int32, device="cuda")[::2])
+    result = verify(**args)
+    args["plan"].synchronize()
+    assert torch.all(backing[:, 1::2] == -777).item()
+    assert result.status.cpu().tolist() == [0, 0]
+
+
+def test_invalid_offsets_do_not_write_tokens():
+    from exactsample_b200.cuda import verify
+    for offsets in [[1, 1, 2], [0, 2, 1], [0, -1, 2], [0, 1, 3]]:
+        args = prepared(np.zeros((2, 4)), [0, 1, 2], np.empty((2, 0)))
+        args["cu_rows"].copy_(__import__("torch").tensor(offsets, device="cuda"))
+        out = verify(**args)
+        args["plan"].synchronize()
+        assert out.status.cpu().tolist() == [int(Status.INVALID_INPUT)] * 2
+        assert out.tokens.cpu().tolist() == [[-1], [-1]]
+
+
+def test_refusals():
+    import torch
+    from exactsample_b200.cuda import CudaRngKey, verify
+    args = prepared(np.zeros((1, 4)), [0, 1], np.empty((1, 0)))
+    with pytest.raises(ValueError, match="mode"):
+        verify(**args, mode="other")
+    with pytest.raises(TypeError):
+        verify(**{**args, "rng": (1, 2, 3)})
+    g = torch.cuda.CUDAGraph()
+    with pytest.raises(RuntimeError, match="graph capture"):
+        with torch.cuda.graph(g):
+            verify(**args)
+    args["plan"].synchronize()
+    assert verify(**args).num_requests == 1
+
+
+def test_fallback_counter_reads_zero_on_plain_rows():
+    case = C.workload_case("C2a", list(range(8)))
+    out, work = run_api(case)
+    assert work.fallbacks() == 0
+    assert (out.status[:8].cpu().numpy() == 0).all()
