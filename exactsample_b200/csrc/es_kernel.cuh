@@ -5,7 +5,7 @@
 namespace es {
 
 constexpr uint32_t BULK_CHUNK = 16384;  // bytes per TMA bulk copy
-constexpr uint32_t WAIT_LIMIT = 1u << 26;  // mbarrier polls before a copy is declared lost
+constexpr uint32_t WAIT_LIMIT = 1u << 22;  // mbarrier polls (about a second) before a copy is declared lost
 
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 

@@ -412,6 +412,7 @@ template <int DT> struct Row {
       }
       exchange();
       // Thread i owns digit 255 - i: merged counts, scanned from the top.
+      if (threadIdx.x == 0) { s.ival[0] = 0; s.ival[1] = 0; }
       int cnt = 0;
       for (int r = 0; r < ranks; ++r) cnt += int(peer(s.hist[parity() ^ 1], r)[255 - threadIdx.x]);
       int total;
@@ -421,7 +422,7 @@ template <int DT> struct Row {
         s.ival[1] = cum - cnt;
       }
       __syncthreads();
-      digit = s.ival[0];
+      digit = s.ival[0] & 255;
       need -= s.ival[1];
       prefix |= Key(digit) << shift;
       known |= Key(255) << shift;
@@ -702,10 +703,11 @@ template <int DT> struct Row {
       }
       bool near = false;
       const bool reach = c > 0 && fx_reaches(above + m_cum, above_n + c_cum, target, &near);
-      if (reach && near) atomicAdd(&diagnostics(p.workspace, p.rows)->near_ties, rank == 0 ? 1u : 0u);
       int first = block_all(reach ? int(threadIdx.x) : INT_MAX, [](int a, int b) { return a < b ? a : b; },
                             s.red.ints);
-      if (first == INT_MAX) first = 255 - last_nonempty();  // unreachable with exact sums; keep the last bucket
+      if (first == INT_MAX)  // only if rounding slack hid the crossing: the last non-empty digit
+        first = block_all(c > 0 ? int(threadIdx.x) : 0, [](int a, int b) { return a > b ? a : b; }, s.red.ints);
+      count_near_tie(block_all(int(int(threadIdx.x) == first && near), [](int a, int b) { return a | b; }, s.red.ints) != 0);
       if (int(threadIdx.x) == first) {
         s.fxval = m_cum - m;
         s.ival[0] = 255 - first;
@@ -750,7 +752,6 @@ template <int DT> struct Row {
     id = cluster_min(owner == rank ? id : INT_MAX);
     return Cut<Key>{1, prefix, id};
   }
-  __device__ int last_nonempty() { return 0; }
 
   // ---- draws ----
   // Certified FP32 argmax of x + G over the valid tokens that `kept` accepts
