@@ -77,9 +77,9 @@ def describe(t) -> Tensor:
         return d
     codes = {torch.float32: ES_F32, torch.float64: ES_F64, torch.float16: ES_F16, torch.bfloat16: ES_BF16,
              torch.int32: ES_I32, torch.int64: ES_I64, torch.uint8: ES_U8}
-    d.data = t.data_ptr()
+    d.data = t.data_ptr() if t.numel() else None
     d.dtype = codes.get(t.dtype, -1)
-    d.ndim = t.dim() if t.dim() <= 2 else -1
+    d.ndim = t.dim() if 0 < t.dim() <= 2 else -1
     for i in range(min(t.dim(), 2)):
         d.size[i] = t.size(i)
         d.stride[i] = t.stride(i)

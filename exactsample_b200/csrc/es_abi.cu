@@ -105,7 +105,7 @@ bool no_internal_overlap(const es_tensor& t) {
   return t.size[0] <= t.stride[1] / divisor || t.size[1] <= t.stride[0] / divisor;
 }
 bool check(const es_tensor& t, int32_t dtype, int ndim, const char* name) {
-  if (t.data == nullptr || t.dtype != dtype || t.ndim != ndim) {
+  if (t.dtype != dtype || t.ndim != ndim || (t.data == nullptr && numel(t) != 0)) {
     g_error = std::string(name) + " has wrong device, dtype or rank";
     return false;
   }
@@ -171,7 +171,8 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
   g_error.clear();
   if (a == nullptr) return fail(ES_ERR_ARGUMENT, "null arguments");
   const es_tensor& logits = a->target_logits;
-  if (logits.data == nullptr || logits.ndim != 2) return fail(ES_ERR_ARGUMENT, "target_logits must be a 2D CUDA tensor");
+  if (logits.ndim != 2 || (logits.data == nullptr && numel(logits) != 0))
+    return fail(ES_ERR_ARGUMENT, "target_logits must be a 2D CUDA tensor");
   if (!is_logit_dtype(logits.dtype))
     return fail(ES_ERR_ARGUMENT, "exactsample logits require float16/bfloat16/float32/float64");
   if (logits.stride[0] < 0 || logits.stride[1] < 0) return fail(ES_ERR_ARGUMENT, "target_logits has a negative stride");
@@ -201,10 +202,11 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
   }
   if (!check(a->positions, ES_I64, 1, "positions")) return ES_ERR_ARGUMENT;
   if (a->positions.size[0] != rows) return fail(ES_ERR_ARGUMENT, "positions must be per target row");
-  const bool has_draft = a->draft_logits.data != nullptr, has_mask = a->mask.data != nullptr;
+  const bool has_draft = a->draft_logits.ndim != 0, has_mask = a->mask.ndim != 0;
   if (has_draft) {
     const es_tensor& q = a->draft_logits;
-    if (q.ndim != 2 || q.size[0] != rows || q.size[1] != vocab || q.stride[0] < 0 || q.stride[1] < 0)
+    if (q.ndim != 2 || q.size[0] != rows || q.size[1] != vocab || q.stride[0] < 0 || q.stride[1] < 0 ||
+        (q.data == nullptr && numel(q) != 0))
       return fail(ES_ERR_ARGUMENT, "draft_logits shape/device mismatch");
     if (q.dtype != logits.dtype) return fail(ES_ERR_ARGUMENT, "draft_logits must have the target_logits dtype");
   }

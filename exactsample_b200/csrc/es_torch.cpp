@@ -30,14 +30,14 @@ int32_t dtype_of(const Tensor& t) {
 
 es_tensor describe(const Tensor& t) {
   es_tensor e{};
-  e.data = const_cast<void*>(t.const_data_ptr());
+  e.data = t.numel() ? const_cast<void*>(t.const_data_ptr()) : nullptr;
   e.dtype = dtype_of(t);
   e.ndim = int32_t(t.dim());
   for (int d = 0; d < t.dim() && d < 2; ++d) {
     e.size[d] = t.size(d);
     e.stride[d] = t.stride(d);
   }
-  if (t.dim() > 2) e.ndim = -1;  // rejected by the C ABI's rank checks
+  if (t.dim() > 2 || t.dim() == 0) e.ndim = -1;  // rejected by the C ABI's rank checks (0 would read as absent)
   return e;
 }
 

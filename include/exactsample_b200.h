@@ -58,8 +58,9 @@ enum es_error {
 };
 
 /* A strided view of at most two dimensions; sizes and strides in elements.
- * A 1-D tensor uses size[0] / stride[0]. data == NULL marks an absent
- * optional tensor (draft_logits, mask). */
+ * A 1-D tensor uses size[0] / stride[0]. A zeroed descriptor (ndim == 0)
+ * marks an absent optional tensor (draft_logits, mask); data may be NULL
+ * only for a tensor with no elements. */
 typedef struct es_tensor {
   void* data;
   int64_t size[2];
