@@ -148,6 +148,7 @@ template <int DT> struct RowKernel {
       int m;
       if (n_keep < valid) {
         m = r.gather_window(n_keep);
+        ES_TRACE(p.workspace, p.rows, r.row, r.rank, 5);
         if (m < 0) {
           const Cut<Key> cut = r.select_nth(n_keep, [](Key, int, W) { return true; });
           m = r.gather_all([&](W v, int t) { return cut.keeps(order_key(v), t); });
@@ -197,6 +198,7 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
   uint32_t* mask_s = reinterpret_cast<uint32_t*>(raw + smem_head<DT>());
   T* slice = reinterpret_cast<T*>(raw + smem_head<DT>() + align_up(4 * size_t(p.slice_words), 128));
   R r(p, s, mask_s, slice);
+  ES_TRACE(p.workspace, p.rows, r.row, r.rank, 0);
 
   // 1. Start copying this rank's slice (and mask words) before waiting for
   //    the preparation kernel: they are inputs, which it never writes.
@@ -226,6 +228,7 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
 
   // 2. The preparation kernel's statuses and counters, then the copy.
   wait_for_prerequisite_grid();
+  ES_TRACE(p.workspace, p.rows, r.row, r.rank, 1);
   bool lost = false;
   for (uint32_t spins = 0; !mbar_try_wait(&s.bar, 0);)
     if (++spins >= WAIT_LIMIT) {
@@ -233,6 +236,7 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
       break;
     }
   lost = __syncthreads_or(lost);
+  ES_TRACE(p.workspace, p.rows, r.row, r.rank, 2);
   if (lost && threadIdx.x == 0) atomicAdd(&diagnostics(p.workspace, p.rows)->wait_timeouts, 1u);
 
   // 3. The row's request and parameters (the same on every rank).
@@ -271,6 +275,7 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
 
   // 4. Validation and the row maximum.
   r.stats_pass(full_q, lost);
+  ES_TRACE(p.workspace, p.rows, r.row, r.rank, 3);
   RowResult res{ES_OK, ES_OK, 0, -1, -1, {0, 0, 0}};
   res.target_status = r.all.bad ? ES_INVALID_INPUT : r.all.valid == 0 ? ES_NO_VALID_TOKEN : ES_OK;
   res.status = res.target_status;
@@ -301,7 +306,9 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
   }
 
   // 6. Publish; the request's last row to finish commits it.
-  r.cluster.sync();  // no rank reads another's shared memory after this point
+  ES_TRACE(p.workspace, p.rows, r.row, r.rank, 6);
+  r.cluster.sync();
+  ES_TRACE(p.workspace, p.rows, r.row, r.rank, 7);  // no rank reads another's shared memory after this point
   if (r.rank == 0 && threadIdx.x == 0) {
     row_results(p.workspace)[r.row] = res;
     __threadfence();

@@ -93,4 +93,19 @@ __host__ __device__ inline uint64_t workspace_needed(int64_t rows) {
 
 template <class T> __device__ __forceinline__ T at(const T* p, int64_t stride, int64_t i) { return p[i * stride]; }
 
+// Phase timestamps for development builds (-DES_TRACE_PHASES): rank r of row
+// `row` stores %globaltimer at phase k in the workspace past every record
+// this file lays out (the reference-sized workspace has room for them).
+#ifdef ES_TRACE_PHASES
+__device__ __forceinline__ void trace_phase(uint8_t* ws, int64_t rows, int row, int rank, int k) {
+  if (threadIdx.x != 0) return;
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  reinterpret_cast<uint64_t*>(ws + 8 + rows * 128)[(int64_t(row) * 16 + rank) * 8 + k] = t;
+}
+#define ES_TRACE(ws, rows, row, rank, k) trace_phase(ws, rows, row, rank, k)
+#else
+#define ES_TRACE(ws, rows, row, rank, k) ((void)0)
+#endif
+
 }  // namespace es

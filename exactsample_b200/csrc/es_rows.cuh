@@ -557,6 +557,7 @@ template <int DT> struct Row {
       }
       if (t >= n && t <= CAP) { pick = i; total = t; offset = before; }
     }
+    ES_TRACE(p.workspace, p.rows, row, rank, 4);
     if (pick < 0) return -1;
     const float width = window_width(pick);
     gather(offset, [&](W v, int) { return float(maxv - v) <= width; });
