@@ -45,7 +45,32 @@ __global__ void __launch_bounds__(128) prepare(const __grid_constant__ Params p)
   p.path[req * p.path_s] = p.exact_draws ? ES_PATH_REFERENCE : ES_PATH_FUSED;
   const int32_t status = bad ? ES_INVALID_INPUT : metadata_status(p, req);
   p.status[req * p.st_s] = status;
-  if (status == ES_OK) arrivals(p.workspace, p.rows)[at(p.cu_rows, p.cu_s, req)] = 0;
+  if (bad) return;  // rows cannot be attributed; the row kernel reads the flag
+  const int64_t begin = at(p.cu_rows, p.cu_s, req), end = at(p.cu_rows, p.cu_s, req + 1);
+  if (begin < 0 || end > p.rows || begin >= end) return;
+  RowCtx c{};
+  c.req = int32_t(req);
+  c.begin = int32_t(begin);
+  c.end = int32_t(end);
+  c.skip = status != ES_OK;
+  if (status == ES_OK) {
+    arrivals(p.workspace, p.rows)[begin] = 0;
+    c.kind = int32_t(at(p.draft_kind, p.kind_s, req));
+    c.top_k = int32_t(at(p.top_k, p.topk_s, req));
+    c.temperature = at(p.temperature, p.temp_s, req);
+    c.top_p = at(p.top_p, p.topp_s, req);
+    c.min_p = at(p.min_p, p.minp_s, req);
+    c.seed = uint64_t(at(p.seeds, p.seed_s, req));
+    c.stream = uint32_t(at(p.streams, p.stream_s, req));
+  }
+  RowCtx* out = row_contexts(p.workspace, p.rows);
+  for (int64_t row = begin; row < end; ++row) {
+    if (status == ES_OK) {
+      c.position = uint32_t(at(p.positions, p.pos_s, row));
+      c.draft_id = row + 1 < end ? int32_t(p.draft_ids[req * p.d_s0 + (row - begin) * p.d_s1]) : -1;
+    }
+    out[row] = c;
+  }
 }
 
 template <int DT> cudaError_t launch_rows(const Params& p, int cluster, cudaStream_t stream);

@@ -12,9 +12,15 @@ __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + 
 template <int DT> __host__ __device__ constexpr size_t smem_head() {
   return align_up(sizeof(Smem<typename Types<DT>::W>), 128);
 }
+// Dynamic shared memory: the header, the slice's mask words, its tile maxima, the slice.
+template <int DT> __host__ __device__ constexpr size_t smem_tmax(int slice_words) {
+  return smem_head<DT>() + align_up(4 * size_t(slice_words), 128);
+}
+template <int DT> __host__ __device__ constexpr size_t smem_slice(int slice_words) {
+  return smem_tmax<DT>(slice_words) + align_up(size_t(slice_words) * sizeof(typename Types<DT>::W), 128);
+}
 template <int DT> __host__ __device__ constexpr size_t smem_bytes(int slice_words) {
-  return smem_head<DT>() + align_up(4 * size_t(slice_words), 128) +
-         align_up(size_t(slice_words) * 32 * sizeof(typename Types<DT>::T), 128);
+  return smem_slice<DT>(slice_words) + align_up(size_t(slice_words) * 32 * sizeof(typename Types<DT>::T), 128);
 }
 
 // The last request whose segment starts at or before `row` (empty segments
@@ -137,7 +143,9 @@ template <int DT> struct RowKernel {
     res.residual = b.id == INT_MAX ? -1 : b.id;
   }
 
-  __device__ static void positive(R& r, const RowCtx& c, bool verify, bool full_q, double sq, RowResult& res,
+  // Returns true when rank 0 finishes the row alone (a list row): the other
+  // ranks may then exit, since no rank touches another's memory afterwards.
+  __device__ static bool positive(R& r, const RowCtx& c, bool verify, bool full_q, double sq, RowResult& res,
                                   const Params& p) {
     const int valid = r.all.valid;
     const int64_t k = c.top_k;
@@ -157,7 +165,7 @@ template <int DT> struct RowKernel {
         m = r.gather_all([](W, int) { return true; });
       }
       if (r.rank == 0) list_finish(r, c, m, n_keep, verify, full_q, sq, u_accept, res);
-      return;
+      return true;
     }
     Cut<Key> cut_k{0, 0, 0}, cut_p{0, 0, 0};
     if (k > 0 && k < valid) cut_k = r.select_nth(int(k), [](Key, int, W) { return true; });
@@ -170,7 +178,7 @@ template <int DT> struct RowKernel {
     auto kept = [cut_k, cut_p](Key key, int t) { return cut_k.keeps(key, t) && cut_p.keeps(key, t); };
     if (!verify) {
       res.sample = r.draw(0, -1, kept, p.exact_draws != 0);
-      return;
+      return false;
     }
     if (!sp_known) sp = r.exact_mass(kept);
     const int x = c.draft_id;
@@ -183,8 +191,9 @@ template <int DT> struct RowKernel {
       }
     }
     res.accept = u_accept < fmin(1.0, px / q_of_draft(r, c, full_q, sq));
-    if (res.accept) return;
+    if (res.accept) return false;
     res.residual = full_q ? r.draw_residual_q(kept, sp, sq) : r.draw(2, x, kept, p.exact_draws != 0);
+    return false;
   }
 };
 
@@ -196,8 +205,9 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
   extern __shared__ __align__(128) uint8_t raw[];
   Smem<W>& s = *reinterpret_cast<Smem<W>*>(raw);
   uint32_t* mask_s = reinterpret_cast<uint32_t*>(raw + smem_head<DT>());
-  T* slice = reinterpret_cast<T*>(raw + smem_head<DT>() + align_up(4 * size_t(p.slice_words), 128));
-  R r(p, s, mask_s, slice);
+  W* tmax = reinterpret_cast<W*>(raw + smem_tmax<DT>(p.slice_words));
+  T* slice = reinterpret_cast<T*>(raw + smem_slice<DT>(p.slice_words));
+  R r(p, s, mask_s, tmax, slice);
   ES_TRACE(p.workspace, p.rows, r.row, r.rank, 0);
 
   // 1. Start copying this rank's slice (and mask words) before waiting for
@@ -239,29 +249,14 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
   ES_TRACE(p.workspace, p.rows, r.row, r.rank, 2);
   if (lost && threadIdx.x == 0) atomicAdd(&diagnostics(p.workspace, p.rows)->wait_timeouts, 1u);
 
-  // 3. The row's request and parameters (the same on every rank).
+  // 3. The row's request and parameters (the same on every rank), gathered
+  //    by the preparation kernel.
   if (threadIdx.x == 0) {
-    RowCtx c{};
-    c.skip = *malformed_flag(p.workspace) != 0;
-    if (!c.skip) {
-      c.req = request_of(p, r.row);
-      c.skip = p.status[int64_t(c.req) * p.st_s] != ES_OK;
+    if (*malformed_flag(p.workspace) != 0) {
+      s.ctx.skip = 1;
+    } else {
+      s.ctx = row_contexts(p.workspace, p.rows)[r.row];
     }
-    if (!c.skip) {
-      const int64_t q = c.req;
-      c.begin = int(at(p.cu_rows, p.cu_s, q));
-      c.end = int(at(p.cu_rows, p.cu_s, q + 1));
-      c.kind = int(at(p.draft_kind, p.kind_s, q));
-      c.draft_id = r.row + 1 < c.end ? int(p.draft_ids[q * p.d_s0 + int64_t(r.row - c.begin) * p.d_s1]) : -1;
-      c.temperature = at(p.temperature, p.temp_s, q);
-      c.top_p = at(p.top_p, p.topp_s, q);
-      c.min_p = at(p.min_p, p.minp_s, q);
-      c.top_k = at(p.top_k, p.topk_s, q);
-      c.seed = uint64_t(at(p.seeds, p.seed_s, q));
-      c.stream = uint32_t(at(p.streams, p.stream_s, q));
-      c.position = uint32_t(at(p.positions, p.pos_s, r.row));
-    }
-    s.ctx = c;
   }
   __syncthreads();
   if (s.ctx.skip) return;  // the same decision on every rank; no rank reads another's memory
@@ -292,6 +287,7 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
   }
 
   // 5. The kept set, the ratio test and the draws.
+  bool solo = false;
   if (res.status == ES_OK) {
     if (c.temperature == 0) {
       K::greedy(r, c, verify, full_q, sq, res);
@@ -301,14 +297,14 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
       r.inv_t = r.slow_x ? 0.f : float(inv);
       r.ln_mp = c.min_p > 0 ? float(log(c.min_p)) : -INFINITY;
       r.mp_tol = c.min_p > 0 ? 1e-6f * (1.f + fabsf(r.ln_mp)) : 0.f;
-      K::positive(r, c, verify, full_q, sq, res, p);
+      solo = K::positive(r, c, verify, full_q, sq, res, p);
     }
   }
 
   // 6. Publish; the request's last row to finish commits it.
   ES_TRACE(p.workspace, p.rows, r.row, r.rank, 6);
-  r.cluster.sync();
-  ES_TRACE(p.workspace, p.rows, r.row, r.rank, 7);  // no rank reads another's shared memory after this point
+  if (!solo) r.cluster.sync();  // no rank reads another's shared memory after this point
+  ES_TRACE(p.workspace, p.rows, r.row, r.rank, 7);
   if (r.rank == 0 && threadIdx.x == 0) {
     row_results(p.workspace)[r.row] = res;
     __threadfence();

@@ -67,6 +67,18 @@ struct RowResult {
 };
 static_assert(sizeof(RowResult) == 32, "RowResult is 32 bytes");
 
+// A row's request and parameters, gathered by the preparation kernel so the
+// row kernel fetches them with one round trip.
+struct alignas(16) RowCtx {
+  int32_t req, begin, end, draft_id, kind, skip;  // skip: the request failed its metadata checks
+  uint32_t stream, position;
+  int32_t top_k, pad0;
+  double temperature, top_p, min_p;
+  uint64_t seed;
+  uint64_t pad1;
+};
+static_assert(sizeof(RowCtx) == 80, "RowCtx is 80 bytes");
+
 // Counters kept after the per-row arrays (reset by the preparation kernel).
 struct Diagnostics {
   uint32_t near_ties;      // exact sums whose rounding sat within the fixed-point slack of a tie
@@ -76,8 +88,8 @@ struct Diagnostics {
 
 // Workspace (bytes): [0] malformed-offsets flag, [4] FP64 recomputation count,
 // [8] RowResult[rows], then one arrival counter per row (used at each
-// request's first row), then Diagnostics. Always within the reference's
-// 8 + rows * (32 + 12288) bytes.
+// request's first row), then Diagnostics, then RowCtx[rows] (16-byte aligned).
+// Always within the reference's 8 + rows * (32 + 12288) bytes.
 __host__ __device__ inline int32_t* malformed_flag(uint8_t* ws) { return reinterpret_cast<int32_t*>(ws); }
 __host__ __device__ inline uint32_t* fallback_count(uint8_t* ws) { return reinterpret_cast<uint32_t*>(ws + 4); }
 __host__ __device__ inline RowResult* row_results(uint8_t* ws) { return reinterpret_cast<RowResult*>(ws + 8); }
@@ -87,8 +99,13 @@ __host__ __device__ inline uint32_t* arrivals(uint8_t* ws, int64_t rows) {
 __host__ __device__ inline Diagnostics* diagnostics(uint8_t* ws, int64_t rows) {
   return reinterpret_cast<Diagnostics*>(ws + 8 + rows * (sizeof(RowResult) + 4));
 }
+__host__ __device__ inline RowCtx* row_contexts(uint8_t* ws, int64_t rows) {
+  const uint64_t at = (8 + rows * (sizeof(RowResult) + 4) + sizeof(Diagnostics) + 15) / 16 * 16;
+  return reinterpret_cast<RowCtx*>(ws + at);
+}
+// Bytes used: at most 8 + 196 * rows + 88 (< the 8 + 12320 * rows provided).
 __host__ __device__ inline uint64_t workspace_needed(int64_t rows) {
-  return rows == 0 ? 8 : uint64_t(8 + rows * (sizeof(RowResult) + 4) + sizeof(Diagnostics));
+  return rows == 0 ? 8 : uint64_t(reinterpret_cast<uintptr_t>(row_contexts(nullptr, rows)) + rows * sizeof(RowCtx));
 }
 
 template <class T> __device__ __forceinline__ T at(const T* p, int64_t stride, int64_t i) { return p[i * stride]; }
@@ -101,7 +118,7 @@ __device__ __forceinline__ void trace_phase(uint8_t* ws, int64_t rows, int row, 
   if (threadIdx.x != 0) return;
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  reinterpret_cast<uint64_t*>(ws + 8 + rows * 128)[(int64_t(row) * 16 + rank) * 8 + k] = t;
+  reinterpret_cast<uint64_t*>(ws + 8 + rows * 256)[(int64_t(row) * 16 + rank) * 8 + k] = t;
 }
 #define ES_TRACE(ws, rows, row, rank, k) trace_phase(ws, rows, row, rank, k)
 #else

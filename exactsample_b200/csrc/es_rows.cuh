@@ -94,17 +94,12 @@ static __device__ __noinline__ bool weight_kept_fp64(double v, double maxv, doub
 }
 
 template <class W> struct Stats {
-  W b1v, b2v, qmax;
-  int32_t b1i, b2i, valid, bad, qvalid, qbad;
+  W b1v, qmax;
+  int32_t b1i, valid, bad, qvalid, qbad;
 };
-
-struct RowCtx {
-  int32_t req, begin, end, draft_id, kind, skip;
-  double temperature, top_p, min_p;
-  int64_t top_k;
-  uint64_t seed;
-  uint32_t stream, position;
-};
+// Candidate tiles (32 tokens) a rank scans for list candidates before it
+// falls back to a full pass.
+constexpr int TILE_CAP = 256;
 
 template <class W> struct Smem {
   uint64_t bar;
@@ -129,6 +124,17 @@ template <class W> struct Smem {
     int32_t win[WARPS][WINDOWS];
     Stats<W> stats[WARPS];
   } red;
+  // Peers' published slots, copied here by a few threads after an exchange.
+  union {
+    Stats<W> stats[16];
+    Pick picks[16];
+    Best bests[16];
+    u128 fx[16];
+    int32_t ints[16 * WINDOWS + 16];
+  } peers;
+  uint32_t peer_n[16];
+  int32_t tiles[TILE_CAP];
+  int32_t n_tiles;
   int32_t ival[4];
   u128 fxval;
   double dval;
@@ -181,6 +187,7 @@ template <int DT> struct Row {
   const Params& p;
   Smem<W>& s;
   uint32_t* mask_s;  // this rank's mask words
+  W* tmax;           // per 32-token tile of the slice: the largest valid value (-inf if none)
   T* slice;          // this rank's logits
   cg::cluster_group cluster;
   int rank, ranks, row, lo, hi, groups;
@@ -194,8 +201,8 @@ template <int DT> struct Row {
   bool slow_x, has_mask;
   Address addr;
 
-  __device__ Row(const Params& p_, Smem<W>& s_, uint32_t* m, T* sl)
-      : p(p_), s(s_), mask_s(m), slice(sl), cluster(cg::this_cluster()) {
+  __device__ Row(const Params& p_, Smem<W>& s_, uint32_t* m, W* tm, T* sl)
+      : p(p_), s(s_), mask_s(m), tmax(tm), slice(sl), cluster(cg::this_cluster()) {
     rank = int(cluster.block_rank());
     ranks = int(cluster.num_blocks());
     row = blockIdx.y;
@@ -282,63 +289,67 @@ template <int DT> struct Row {
 
   // ---- the statistics pass ----
   __device__ static Stats<W> merge_stats(Stats<W> a, Stats<W> b) {
-    auto better = [](W av, int ai, W bv, int bi) { return av > bv || (av == bv && ai < bi); };
-    const bool b_first = better(b.b1v, b.b1i, a.b1v, a.b1i);
-    const W w1 = b_first ? b.b1v : a.b1v, l1 = b_first ? a.b1v : b.b1v, w2 = b_first ? b.b2v : a.b2v;
-    const int w1i = b_first ? b.b1i : a.b1i, l1i = b_first ? a.b1i : b.b1i, w2i = b_first ? b.b2i : a.b2i;
-    Stats<W> r;
-    r.b1v = w1;
-    r.b1i = w1i;
-    const bool l_second = better(l1, l1i, w2, w2i);
-    r.b2v = l_second ? l1 : w2;
-    r.b2i = l_second ? l1i : w2i;
-    r.qmax = a.qmax > b.qmax ? a.qmax : b.qmax;
-    r.valid = a.valid + b.valid;
-    r.bad = a.bad | b.bad;
-    r.qvalid = a.qvalid + b.qvalid;
-    r.qbad = a.qbad | b.qbad;
-    return r;
+    const bool b_first = b.b1v > a.b1v || (b.b1v == a.b1v && b.b1i < a.b1i);
+    Stats<W> m;
+    m.b1v = b_first ? b.b1v : a.b1v;
+    m.b1i = b_first ? b.b1i : a.b1i;
+    m.qmax = a.qmax > b.qmax ? a.qmax : b.qmax;
+    m.valid = a.valid + b.valid;
+    m.bad = a.bad | b.bad;
+    m.qvalid = a.qvalid + b.qvalid;
+    m.qbad = a.qbad | b.qbad;
+    return m;
   }
   __device__ Stats<W> block_stats(Stats<W> v) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
       Stats<W> y;
-      y.b1v = shfl_xor(v.b1v, o); y.b2v = shfl_xor(v.b2v, o); y.qmax = shfl_xor(v.qmax, o);
-      y.b1i = shfl_xor(v.b1i, o); y.b2i = shfl_xor(v.b2i, o); y.valid = shfl_xor(v.valid, o);
-      y.bad = shfl_xor(v.bad, o); y.qvalid = shfl_xor(v.qvalid, o); y.qbad = shfl_xor(v.qbad, o);
+      y.b1v = shfl_xor(v.b1v, o); y.qmax = shfl_xor(v.qmax, o); y.b1i = shfl_xor(v.b1i, o);
+      y.valid = shfl_xor(v.valid, o); y.bad = shfl_xor(v.bad, o); y.qvalid = shfl_xor(v.qvalid, o);
+      y.qbad = shfl_xor(v.qbad, o);
       v = merge_stats(v, y);
     }
     if (lane_id() == 0) s.red.stats[warp_id()] = v;
     __syncthreads();
-    Stats<W> r = s.red.stats[0];
-    for (int w = 1; w < WARPS; ++w) r = merge_stats(r, s.red.stats[w]);
+    Stats<W> m = s.red.stats[0];
+    for (int w = 1; w < WARPS; ++w) m = merge_stats(m, s.red.stats[w]);
     __syncthreads();
-    return r;
+    return m;
   }
-  // NaN / +inf anywhere (even masked), the count of valid tokens, the
-  // maximum with the lowest ID among equals, the runner-up, and for a full-q
-  // draft row the same checks of the proposal row.
+  // NaN / +inf anywhere in the slice (even masked), the count of valid
+  // tokens, the maximum with the lowest ID among equals, each 32-token tile's
+  // maximum, and for a full-q draft row the same checks of the proposal row.
+  // Warp-uniform loop: the 8 lanes of a tile combine its maximum by shuffles.
   __device__ void stats_pass(bool full_q, bool timed_out) {
-    W b1v = W(-INFINITY), b2v = W(-INFINITY), qmax = W(-INFINITY);
-    int b1i = INT_MAX, b2i = INT_MAX, nvalid = 0, bad = 0, qvalid = 0, qbad = 0;
-    for (int g = threadIdx.x; g < groups; g += THREADS) {
-      W v[4];
-      load4(slice + 4 * g, v);
-      const unsigned bits = group_bits(g);
-      const int inside = min(4, hi - lo - 4 * g);
+    W best = W(-INFINITY), qmax = W(-INFINITY);
+    int best_i = INT_MAX, nvalid = 0, bad = 0, qvalid = 0, qbad = 0;
+    for (int base = warp_id() * 32; base < groups; base += THREADS) {
+      const int g = base + lane_id();
+      W tile = W(-INFINITY);
+      if (g < groups) {
+        W v[4];
+        load4(slice + 4 * g, v);
+        const unsigned bits = group_bits(g);
+        const int inside = min(4, hi - lo - 4 * g);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (j >= inside) break;
-        bad |= isnan(v[j]) | (v[j] == W(INFINITY));
-        const bool ok = ((bits >> j) & 1u) && v[j] > W(-INFINITY);
-        nvalid += ok;
-        const int t = lo + 4 * g + j;
-        if (ok && v[j] > b1v) {  // IDs rise within a thread, so ties keep the lowest
-          b2v = b1v; b2i = b1i; b1v = v[j]; b1i = t;
-        } else if (ok && v[j] > b2v) {
-          b2v = v[j]; b2i = t;
+        for (int j = 0; j < 4; ++j) {
+          if (j < inside) bad |= !(v[j] < W(INFINITY)) & (v[j] != W(-INFINITY));  // NaN or +inf
+          const bool ok = ((bits >> j) & 1u) && v[j] > W(-INFINITY);
+          const W x = ok ? v[j] : W(-INFINITY);
+          nvalid += ok;
+          if (x > best) {  // IDs rise within a thread, so ties keep the lowest
+            best = x;
+            best_i = lo + 4 * g + j;
+          }
+          tile = x > tile ? x : tile;
         }
       }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        const W other = shfl_xor(tile, o);
+        tile = other > tile ? other : tile;
+      }
+      if ((lane_id() & 7) == 0 && g < groups) tmax[g >> 3] = tile;
     }
     if (full_q)
       for (int t = lo + int(threadIdx.x); t < hi; t += THREADS) {
@@ -348,12 +359,15 @@ template <int DT> struct Row {
         qmax = y > qmax ? y : qmax;
       }
     if (timed_out) bad = 1;  // this rank's slice never arrived: the row is not trusted
-    const Stats<W> merged = block_stats(Stats<W>{b1v, b2v, qmax, b1i, b2i, nvalid, bad, qvalid, qbad});
+    const Stats<W> merged = block_stats(Stats<W>{best, qmax, best_i, nvalid, bad, qvalid, qbad});
     if (threadIdx.x == 0) s.stats[parity()] = merged;
     exchange();
-    all = *peer(&s.stats[parity() ^ 1], 0);
-    for (int r = 1; r < ranks; ++r) all = merge_stats(all, *peer(&s.stats[parity() ^ 1], r));
+    if (int(threadIdx.x) < ranks) s.peers.stats[threadIdx.x] = *peer(&s.stats[parity() ^ 1], threadIdx.x);
+    __syncthreads();
+    all = s.peers.stats[0];
+    for (int r = 1; r < ranks; ++r) all = merge_stats(all, s.peers.stats[r]);
     maxv = all.b1v;
+    __syncthreads();
   }
 
   // ---- cluster-wide reductions ----
@@ -365,22 +379,44 @@ template <int DT> struct Row {
       s.fxn[parity()] = bn;
     }
     exchange();
+    if (int(threadIdx.x) < ranks) {
+      s.peers.fx[threadIdx.x] = *peer(&s.fx[parity() ^ 1], threadIdx.x);
+      s.peer_n[threadIdx.x] = *peer(&s.fxn[parity() ^ 1], threadIdx.x);
+    }
+    __syncthreads();
     u128 total = 0;
     uint32_t n = 0;
     for (int r = 0; r < ranks; ++r) {
-      total += *peer(&s.fx[parity() ^ 1], r);
-      n += *peer(&s.fxn[parity() ^ 1], r);
+      total += s.peers.fx[r];
+      n += s.peer_n[r];
     }
     *n_total = n;
+    __syncthreads();
     return total;
   }
   __device__ int cluster_min(int local) {
     const int b = block_all(local, [](int a, int c) { return a < c ? a : c; }, s.red.ints);
     if (threadIdx.x == 0) s.slot[parity()] = b;
     exchange();
+    if (int(threadIdx.x) < ranks) s.peers.ints[threadIdx.x] = *peer(&s.slot[parity() ^ 1], threadIdx.x);
+    __syncthreads();
     int m = INT_MAX;
-    for (int r = 0; r < ranks; ++r) m = min(m, *peer(&s.slot[parity() ^ 1], r));
+    for (int r = 0; r < ranks; ++r) m = min(m, s.peers.ints[r]);
+    __syncthreads();
     return m;
+  }
+
+  // The FP64 argmax over the cluster (lowest ID on ties); -1 if empty.
+  __device__ int cluster_best(Best b) {
+    b = block_all(b, [](Best a, Best c) { return best_of(a, c); }, s.red.bests);
+    if (threadIdx.x == 0) s.best[parity()] = b;
+    exchange();
+    if (int(threadIdx.x) < ranks) s.peers.bests[threadIdx.x] = *peer(&s.best[parity() ^ 1], threadIdx.x);
+    __syncthreads();
+    Best winner = no_best();
+    for (int r = 0; r < ranks; ++r) winner = best_of(winner, s.peers.bests[r]);
+    __syncthreads();
+    return winner.id == INT_MAX ? -1 : winner.id;
   }
 
   // ---- radix selection (integer, exact) ----
@@ -510,22 +546,39 @@ template <int DT> struct Row {
     c = block_all(c, [](int a, int b) { return a + b; }, s.red.ints);
     if (threadIdx.x == 0) s.slot[parity()] = c;
     exchange();
+    if (int(threadIdx.x) < ranks) s.peers.ints[threadIdx.x] = *peer(&s.slot[parity() ^ 1], threadIdx.x);
+    __syncthreads();
     int total = 0, offset = 0;
     for (int r = 0; r < ranks; ++r) {
-      const int cr = *peer(&s.slot[parity() ^ 1], r);
+      const int cr = s.peers.ints[r];
       total += cr;
       if (r < rank) offset += cr;
     }
+    __syncthreads();
     if (total <= CAP) gather(offset, take);
     return total;
   }
   // The top-n valid tokens (and ties at the n-th value) near the maximum:
-  // the narrowest distance window below the maximum that holds at least n
-  // tokens and at most CAP is gathered to rank 0. Returns the count, or -1
-  // if no window qualifies.
+  // the narrowest distance window below the maximum (0.25 to 32 logits) that
+  // holds at least n tokens and at most CAP is gathered to rank 0. Only tiles
+  // whose maximum is within 32 of the row's are scanned, unless some rank has
+  // more than TILE_CAP of them (a flat row), which scans its whole slice.
+  // Returns the count, or -1 if no window qualifies.
   __device__ int gather_window(int n) {
+    // This rank's candidate tiles.
+    if (threadIdx.x == 0) s.n_tiles = 0;
+    __syncthreads();
+    const int n_tiles_all = (groups + 7) / 8;
+    for (int t = threadIdx.x; t < n_tiles_all; t += THREADS)
+      if (float(maxv - tmax[t]) <= window_width(WINDOWS - 1)) {
+        const int at_ = atomicAdd(&s.n_tiles, 1);
+        if (at_ < TILE_CAP) s.tiles[at_] = t;
+      }
+    __syncthreads();
+    const int cand = s.n_tiles;
+    const bool whole = cand > TILE_CAP;
     int c[WINDOWS] = {};
-    for (int g = threadIdx.x; g < groups; g += THREADS) {
+    auto count = [&](int g) {
       W v[4];
       const unsigned bits = group(g, v);
 #pragma unroll
@@ -534,6 +587,14 @@ template <int DT> struct Row {
         const float d = float(maxv - v[j]);  // monotone in v
 #pragma unroll
         for (int i = 0; i < WINDOWS; ++i) c[i] += d <= window_width(i);
+      }
+    };
+    if (whole) {
+      for (int g = threadIdx.x; g < groups; g += THREADS) count(g);
+    } else {
+      for (int k = threadIdx.x; k < cand * 8; k += THREADS) {
+        const int g = s.tiles[k >> 3] * 8 + (k & 7);
+        if (g < groups) count(g);
       }
     }
 #pragma unroll
@@ -547,20 +608,51 @@ template <int DT> struct Row {
       s.wcount[parity()][threadIdx.x] = t;
     }
     exchange();
+    if (int(threadIdx.x) < ranks * WINDOWS) {
+      const int rr = threadIdx.x / WINDOWS, i = threadIdx.x % WINDOWS;
+      s.peers.ints[threadIdx.x] = peer(s.wcount[parity() ^ 1], rr)[i];
+    }
+    __syncthreads();
     int pick = -1, total = 0, offset = 0;
     for (int i = 0; i < WINDOWS && pick < 0; ++i) {
       int t = 0, before = 0;
-      for (int r = 0; r < ranks; ++r) {
-        const int cr = peer(s.wcount[parity() ^ 1], r)[i];
+      for (int rr = 0; rr < ranks; ++rr) {
+        const int cr = s.peers.ints[rr * WINDOWS + i];
         t += cr;
-        if (r < rank) before += cr;
+        if (rr < rank) before += cr;
       }
       if (t >= n && t <= CAP) { pick = i; total = t; offset = before; }
     }
     ES_TRACE(p.workspace, p.rows, row, rank, 4);
+    __syncthreads();
     if (pick < 0) return -1;
     const float width = window_width(pick);
-    gather(offset, [&](W v, int) { return float(maxv - v) <= width; });
+    if (threadIdx.x == 0) s.n_cand = 0;
+    __syncthreads();
+    uint64_t* keys = peer(s.u.cand.key, 0);
+    int32_t* ids = peer(s.u.cand.id, 0);
+    auto take = [&](int g) {
+      W v[4];
+      const unsigned bits = group(g, v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (!((bits >> j) & 1u) || !(float(maxv - v[j]) <= width)) continue;
+        const int at_ = offset + atomicAdd(&s.n_cand, 1);
+        if (at_ < CAP) {
+          keys[at_] = uint64_t(order_key(v[j]));
+          ids[at_] = lo + 4 * g + j;
+        }
+      }
+    };
+    if (whole) {
+      for (int g = threadIdx.x; g < groups; g += THREADS) take(g);
+    } else {
+      for (int k = threadIdx.x; k < cand * 8; k += THREADS) {
+        const int g = s.tiles[k >> 3] * 8 + (k & 7);
+        if (g < groups) take(g);
+      }
+    }
+    exchange();
     return total;
   }
 
@@ -764,7 +856,7 @@ template <int DT> struct Row {
       // A kept token's score bounds the winner's from below: the maximum
       // (x = 0), or the runner-up when the maximum is excluded.
       float floor = -INFINITY;
-      const int t = all.b1i != excluded ? all.b1i : all.b2i;
+      const int t = all.b1i != excluded ? all.b1i : INT_MAX;
       if (t != INT_MAX && valid_global(t)) {
         const W v = value_global(t);
         const float x = x32(v);
@@ -822,8 +914,11 @@ template <int DT> struct Row {
     best = block_all(best, [](Pick a, Pick b) { return pick_of(a, b); }, s.red.picks);
     if (threadIdx.x == 0) s.pick[parity()] = best;
     exchange();
+    if (int(threadIdx.x) < ranks) s.peers.picks[threadIdx.x] = *peer(&s.pick[parity() ^ 1], threadIdx.x);
+    __syncthreads();
     Pick top = no_pick();
-    for (int r = 0; r < ranks; ++r) top = pick_of(top, *peer(&s.pick[parity() ^ 1], r));
+    for (int r = 0; r < ranks; ++r) top = pick_of(top, s.peers.picks[r]);
+    __syncthreads();
     if (!exact_only) {
       if (top.id == INT_MAX) return -1;
       if (top.lo > top.others) return top.id;
@@ -859,12 +954,7 @@ template <int DT> struct Row {
         b = best_of(b, Best{x64(v[j]) + noise64(r.w[j]), lo + 4 * g + j});
       }
     }
-    b = block_all(b, [](Best a, Best c) { return best_of(a, c); }, s.red.bests);
-    if (threadIdx.x == 0) s.best[parity()] = b;
-    exchange();
-    Best winner = no_best();
-    for (int r = 0; r < ranks; ++r) winner = best_of(winner, *peer(&s.best[parity() ^ 1], r));
-    return winner.id == INT_MAX ? -1 : winner.id;
+    return cluster_best(b);
   }
 
   // The residual draw max(p - q, 0) of a full-q draft row over the kept set,
@@ -894,12 +984,7 @@ template <int DT> struct Row {
       for (int j = 0; j < 4; ++j)
         if (r4[j] > 0) b = best_of(b, Best{log(r4[j]) + noise64(r.w[j]), lo + 4 * g + j});
     }
-    b = block_all(b, [](Best a, Best c) { return best_of(a, c); }, s.red.bests);
-    if (threadIdx.x == 0) s.best[parity()] = b;
-    exchange();
-    Best winner = no_best();
-    for (int r = 0; r < ranks; ++r) winner = best_of(winner, *peer(&s.best[parity() ^ 1], r));
-    return winner.id == INT_MAX ? -1 : winner.id;
+    return cluster_best(b);
   }
 };
 
