@@ -71,6 +71,7 @@ template <int DT> struct RowKernel {
                                      double u_accept, RowResult& res) {
     auto& s = r.s;
     r.sort_candidates(m);
+    ES_TRACE(r.p.workspace, r.p.rows, r.row, r.rank, 10);
     const int i = threadIdx.x;
     const bool in = i < n_keep;
     const int id = in ? s.u.cand.id[i] : INT_MAX;
@@ -108,6 +109,7 @@ template <int DT> struct RowKernel {
       r.count_near_tie(near);
       __syncthreads();
     }
+    ES_TRACE(r.p.workspace, r.p.rows, r.row, r.rank, 11);
     const double prob = i < n2 ? w / denominator : 0.0;
     if (i < LIST_MAX) s.lp[i] = prob;
     __syncthreads();
@@ -120,6 +122,7 @@ template <int DT> struct RowKernel {
     };
     if (!verify) {
       res.sample = draw_list(0, -1);
+      ES_TRACE(r.p.workspace, r.p.rows, r.row, r.rank, 12);
       return;
     }
     const int at_draft = block_all(i < n2 && id == c.draft_id ? i : INT_MAX, [](int a, int b) { return a < b ? a : b; },
@@ -155,7 +158,7 @@ template <int DT> struct RowKernel {
     if (n_keep <= list_max) {
       int m;
       if (n_keep < valid) {
-        m = r.gather_window(n_keep);
+        m = r.gather_near(n_keep);
         ES_TRACE(p.workspace, p.rows, r.row, r.rank, 5);
         if (m < 0) {
           const Cut<Key> cut = r.select_nth(n_keep, [](Key, int, W) { return true; });

@@ -118,7 +118,7 @@ __device__ __forceinline__ void trace_phase(uint8_t* ws, int64_t rows, int row, 
   if (threadIdx.x != 0) return;
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  reinterpret_cast<uint64_t*>(ws + 8 + rows * 256)[(int64_t(row) * 16 + rank) * 8 + k] = t;
+  reinterpret_cast<uint64_t*>(ws + 8 + rows * 256)[(int64_t(row) * 16 + rank) * 16 + k] = t;
 }
 #define ES_TRACE(ws, rows, row, rank, k) trace_phase(ws, rows, row, rank, k)
 #else

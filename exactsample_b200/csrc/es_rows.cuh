@@ -133,6 +133,7 @@ template <class W> struct Smem {
     int32_t ints[16 * WINDOWS + 16];
   } peers;
   uint32_t peer_n[16];
+  int32_t pushed[16];  // per-rank counts each rank writes into every rank's copy
   int32_t tiles[TILE_CAP];
   int32_t n_tiles;
   int32_t ival[4];
@@ -361,7 +362,9 @@ template <int DT> struct Row {
     if (timed_out) bad = 1;  // this rank's slice never arrived: the row is not trusted
     const Stats<W> merged = block_stats(Stats<W>{best, qmax, best_i, nvalid, bad, qvalid, qbad});
     if (threadIdx.x == 0) s.stats[parity()] = merged;
+    ES_TRACE(p.workspace, p.rows, row, rank, 8);
     exchange();
+    ES_TRACE(p.workspace, p.rows, row, rank, 9);
     if (int(threadIdx.x) < ranks) s.peers.stats[threadIdx.x] = *peer(&s.stats[parity() ^ 1], threadIdx.x);
     __syncthreads();
     all = s.peers.stats[0];
@@ -558,102 +561,69 @@ template <int DT> struct Row {
     if (total <= CAP) gather(offset, take);
     return total;
   }
-  // The top-n valid tokens (and ties at the n-th value) near the maximum:
-  // the narrowest distance window below the maximum (0.25 to 32 logits) that
-  // holds at least n tokens and at most CAP is gathered to rank 0. Only tiles
-  // whose maximum is within 32 of the row's are scanned, unless some rank has
-  // more than TILE_CAP of them (a flat row), which scans its whole slice.
-  // Returns the count, or -1 if no window qualifies.
-  __device__ int gather_window(int n) {
-    // This rank's candidate tiles.
-    if (threadIdx.x == 0) s.n_tiles = 0;
-    __syncthreads();
-    const int n_tiles_all = (groups + 7) / 8;
-    for (int t = threadIdx.x; t < n_tiles_all; t += THREADS)
-      if (float(maxv - tmax[t]) <= window_width(WINDOWS - 1)) {
-        const int at_ = atomicAdd(&s.n_tiles, 1);
-        if (at_ < TILE_CAP) s.tiles[at_] = t;
-      }
-    __syncthreads();
-    const int cand = s.n_tiles;
-    const bool whole = cand > TILE_CAP;
-    int c[WINDOWS] = {};
-    auto count = [&](int g) {
-      W v[4];
-      const unsigned bits = group(g, v);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (!((bits >> j) & 1u)) continue;
-        const float d = float(maxv - v[j]);  // monotone in v
-#pragma unroll
-        for (int i = 0; i < WINDOWS; ++i) c[i] += d <= window_width(i);
-      }
-    };
-    if (whole) {
-      for (int g = threadIdx.x; g < groups; g += THREADS) count(g);
-    } else {
-      for (int k = threadIdx.x; k < cand * 8; k += THREADS) {
-        const int g = s.tiles[k >> 3] * 8 + (k & 7);
-        if (g < groups) count(g);
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < WINDOWS; ++i) c[i] = warp_all(c[i], [](int a, int b) { return a + b; });
-    if (lane_id() == 0)
-      for (int i = 0; i < WINDOWS; ++i) s.red.win[warp_id()][i] = c[i];
-    __syncthreads();
-    if (threadIdx.x < WINDOWS) {
-      int t = 0;
-      for (int w = 0; w < WARPS; ++w) t += s.red.win[w][threadIdx.x];
-      s.wcount[parity()][threadIdx.x] = t;
-    }
-    exchange();
-    if (int(threadIdx.x) < ranks * WINDOWS) {
-      const int rr = threadIdx.x / WINDOWS, i = threadIdx.x % WINDOWS;
-      s.peers.ints[threadIdx.x] = peer(s.wcount[parity() ^ 1], rr)[i];
-    }
-    __syncthreads();
-    int pick = -1, total = 0, offset = 0;
-    for (int i = 0; i < WINDOWS && pick < 0; ++i) {
-      int t = 0, before = 0;
-      for (int rr = 0; rr < ranks; ++rr) {
-        const int cr = s.peers.ints[rr * WINDOWS + i];
-        t += cr;
-        if (rr < rank) before += cr;
-      }
-      if (t >= n && t <= CAP) { pick = i; total = t; offset = before; }
-    }
-    ES_TRACE(p.workspace, p.rows, row, rank, 4);
-    __syncthreads();
-    if (pick < 0) return -1;
-    const float width = window_width(pick);
+  // Distance below the row maximum in 0.5-logit bins (DIST_BINS: 64 or more).
+  __device__ __forceinline__ int dist_bin(W v) const {
+    const float d = float(maxv - v);  // monotone in v
+    return d < float(DIST_BINS / 2) ? int(d * 2.f) : DIST_BINS;
+  }
+  // The top-n valid tokens (and every token tied with the n-th) gathered to
+  // rank 0. The ranks histogram their 32-token tiles by the distance of each
+  // tile's maximum below the row's; the first bin b where the cumulative tile
+  // count reaches n bounds the n-th token (every such tile has a token within
+  // bin b), so every valid token with bin <= b is gathered, from those tiles
+  // only. Slots in rank 0's buffer come from an atomic counter there; each
+  // rank pushes its count to every rank before the closing exchange. Returns
+  // the count, or -1 if no bin below 64 logits qualifies or the tokens do not
+  // fit the buffer (the caller then radix-selects).
+  __device__ int gather_near(int n) {
+    uint32_t* h = s.hist[parity()];
+    for (int i = threadIdx.x; i < RADIX; i += THREADS) h[i] = 0;
     if (threadIdx.x == 0) s.n_cand = 0;
     __syncthreads();
+    const int n_tiles = (groups + 7) / 8;
+    for (int base = warp_id() * 32; base < n_tiles; base += THREADS) {
+      const int t = base + lane_id();
+      const int b = t < n_tiles && tmax[t] > W(-INFINITY) ? min(dist_bin(tmax[t]), DIST_BINS) : -1;
+      warp_bucket_add(nullptr, h, b, 0);
+    }
+    exchange();
+    int cnt = 0;
+    if (int(threadIdx.x) < DIST_BINS)
+      for (int rr = 0; rr < ranks; ++rr) cnt += int(peer(s.hist[parity() ^ 1], rr)[threadIdx.x]);
+    int total;
+    const int cum = block_scan(cnt, s.red.ints, &total);
+    if (threadIdx.x == 0) s.ival[0] = -1;
+    __syncthreads();
+    if (cum >= n && cum - cnt < n) s.ival[0] = threadIdx.x;
+    __syncthreads();
+    const int window = s.ival[0];
+    ES_TRACE(p.workspace, p.rows, row, rank, 4);
+    if (window < 0) return -1;
+    int* counter = peer(&s.n_cand, 0);
     uint64_t* keys = peer(s.u.cand.key, 0);
     int32_t* ids = peer(s.u.cand.id, 0);
-    auto take = [&](int g) {
+    int mine = 0;
+    for (int g = threadIdx.x; g < groups; g += THREADS) {
+      if (dist_bin(tmax[g >> 3]) > window) continue;  // the tile's maximum is farther: so are its tokens
       W v[4];
       const unsigned bits = group(g, v);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        if (!((bits >> j) & 1u) || !(float(maxv - v[j]) <= width)) continue;
-        const int at_ = offset + atomicAdd(&s.n_cand, 1);
+        if (!((bits >> j) & 1u) || dist_bin(v[j]) > window) continue;
+        ++mine;
+        const int at_ = atomicAdd(counter, 1);
         if (at_ < CAP) {
           keys[at_] = uint64_t(order_key(v[j]));
           ids[at_] = lo + 4 * g + j;
         }
       }
-    };
-    if (whole) {
-      for (int g = threadIdx.x; g < groups; g += THREADS) take(g);
-    } else {
-      for (int k = threadIdx.x; k < cand * 8; k += THREADS) {
-        const int g = s.tiles[k >> 3] * 8 + (k & 7);
-        if (g < groups) take(g);
-      }
     }
+    mine = block_all(mine, [](int a, int b) { return a + b; }, s.red.ints);
+    if (int(threadIdx.x) < ranks) peer(s.pushed, threadIdx.x)[rank] = mine;
     exchange();
-    return total;
+    int gathered = 0;
+    for (int rr = 0; rr < ranks; ++rr) gathered += s.pushed[rr];
+    return gathered <= CAP ? gathered : -1;
   }
 
   // Sorts rank 0's m candidates into (key desc, ID asc) order (bitonic).
