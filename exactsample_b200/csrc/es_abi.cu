@@ -143,38 +143,62 @@ bool check(const es_tensor& t, int32_t dtype, int ndim, const char* name) {
 }
 bool is_logit_dtype(int32_t d) { return d == ES_F32 || d == ES_F64 || d == ES_F16 || d == ES_BF16; }
 
-// Cluster ranks per row: about TOKENS_PER_RANK tokens per rank, more ranks for
-// small batches (a single row spreads over 16 SMs), and at most MAX_SLICE
-// bytes of shared memory per rank.
-constexpr int64_t TOKENS_PER_RANK = 19000;
+// Ranks per row and the row mode.
+//   * Resident rows: each rank keeps its slice (about RESIDENT_BYTES) in
+//     shared memory, so later passes never touch HBM; chosen when every
+//     row's cluster fits on the GPU at once (small batches), with as many
+//     ranks per row as that allows (up to 16) to spread a row over SMs.
+//   * Streamed rows: each rank streams its slice through a TMA ring and later
+//     passes re-read global memory (L2); one rank per row from 148 rows on,
+//     so a large batch runs in one wave with no cluster barriers.
+constexpr size_t RESIDENT_BYTES = 80 * 1024;
+constexpr int SM_COUNT = 148, RESIDENT_SLOTS = 2 * SM_COUNT;
 constexpr size_t MAX_SMEM = 227 * 1024;
 
-int choose_cluster(int64_t rows, int64_t vocab, int dtype, int* slice_words, size_t* smem) {
+template <int DT> size_t smem_for(int sw, bool stream) { return es::smem_bytes<DT>(sw, stream); }
+size_t smem_for_dtype(int dtype, int sw, bool stream) {
+  switch (dtype) {
+    case ES_F32: return smem_for<ES_F32>(sw, stream);
+    case ES_F64: return smem_for<ES_F64>(sw, stream);
+    case ES_F16: return smem_for<ES_F16>(sw, stream);
+    default: return smem_for<ES_BF16>(sw, stream);
+  }
+}
+
+int choose_cluster(int64_t rows, int64_t vocab, int dtype, int* slice_words, size_t* smem, int* stream) {
   const int64_t words = (vocab + 31) / 32;
-  int c = int(std::min<int64_t>(16, std::max<int64_t>(1, (vocab + TOKENS_PER_RANK - 1) / TOKENS_PER_RANK)));
-  if (rows <= 16 && vocab >= 4096) c = 16;
-  else if (rows <= 48 && vocab >= 4096) c = std::max(c, 8);
+  const size_t row_bytes = size_t(vocab) * element_size(dtype);
+  const int resident_min = int(std::max<size_t>(1, (row_bytes + RESIDENT_BYTES - 1) / RESIDENT_BYTES));
+  int c;
+  bool streamed;
+  if (resident_min <= 16 && rows * resident_min <= RESIDENT_SLOTS) {
+    streamed = false;
+    c = int(std::min<int64_t>(16, std::max<int64_t>(resident_min, RESIDENT_SLOTS / std::max<int64_t>(rows, 1))));
+    if (vocab < 4096) c = resident_min;  // tiny rows: one rank
+  } else {
+    streamed = true;
+    c = int(std::min<int64_t>(16, std::max<int64_t>(1, SM_COUNT / std::max<int64_t>(rows, 1))));
+  }
   // EXACTSAMPLE_CLUSTER=n asks for n ranks per row (1..16), e.g. to show that
-  // results do not depend on the split; shared memory limits may raise it.
+  // results do not depend on the split; EXACTSAMPLE_STREAM=0/1 forces the row
+  // mode. Shared-memory limits may raise the rank count.
   if (const char* forced = std::getenv("EXACTSAMPLE_CLUSTER")) {
     const int n = std::atoi(forced);
     if (n >= 1 && n <= 16) c = n;
   }
-  auto bytes = [&](int sw) {
-    switch (dtype) {
-      case ES_F32: return es::smem_bytes<ES_F32>(sw);
-      case ES_F64: return es::smem_bytes<ES_F64>(sw);
-      case ES_F16: return es::smem_bytes<ES_F16>(sw);
-      default: return es::smem_bytes<ES_BF16>(sw);
-    }
-  };
+  if (const char* forced = std::getenv("EXACTSAMPLE_STREAM")) {
+    if (forced[0] == '0') streamed = false;
+    if (forced[0] == '1') streamed = true;
+  }
   for (;; ++c) {
     if (c > 16) return -1;
     const int sw = int((words + c - 1) / c);
     const int used = int((words + sw - 1) / sw);  // no empty ranks
-    if (bytes(sw) <= MAX_SMEM) {
+    const size_t bytes = smem_for_dtype(dtype, sw, streamed);
+    if (bytes <= MAX_SMEM) {
       *slice_words = sw;
-      *smem = bytes(sw);
+      *smem = bytes;
+      *stream = streamed;
       return used;
     }
   }
@@ -305,7 +329,7 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
   int cluster = 1;
   size_t smem = 0;
   if (rows > 0) {
-    cluster = choose_cluster(rows, vocab, logits.dtype, &p.slice_words, &smem);
+    cluster = choose_cluster(rows, vocab, logits.dtype, &p.slice_words, &smem, &p.stream_rows);
     if (cluster < 0) return fail(ES_ERR_UNSUPPORTED, "vocabulary too large for one 16-block cluster's shared memory");
     const size_t e = element_size(logits.dtype);
     p.vector_load = logits.stride[1] == 1 && reinterpret_cast<uintptr_t>(logits.data) % 16 == 0 &&

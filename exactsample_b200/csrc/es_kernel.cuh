@@ -12,15 +12,18 @@ __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + 
 template <int DT> __host__ __device__ constexpr size_t smem_head() {
   return align_up(sizeof(Smem<typename Types<DT>::W>), 128);
 }
-// Dynamic shared memory: the header, the slice's mask words, its tile maxima, the slice.
-template <int DT> __host__ __device__ constexpr size_t smem_tmax(int slice_words) {
-  return smem_head<DT>() + align_up(4 * size_t(slice_words), 128);
+// Dynamic shared memory: the header, the slice's mask words (resident rows),
+// its tile maxima, then the slice itself (resident) or the TMA ring (streamed).
+template <int DT> __host__ __device__ constexpr size_t smem_tmax(int slice_words, bool stream) {
+  return smem_head<DT>() + (stream ? 0 : align_up(4 * size_t(slice_words), 128));
 }
-template <int DT> __host__ __device__ constexpr size_t smem_slice(int slice_words) {
-  return smem_tmax<DT>(slice_words) + align_up(size_t(slice_words) * sizeof(typename Types<DT>::W), 128);
+template <int DT> __host__ __device__ constexpr size_t smem_slice(int slice_words, bool stream) {
+  return smem_tmax<DT>(slice_words, stream) + align_up(size_t(slice_words) * sizeof(typename Types<DT>::W), 128);
 }
-template <int DT> __host__ __device__ constexpr size_t smem_bytes(int slice_words) {
-  return smem_slice<DT>(slice_words) + align_up(size_t(slice_words) * 32 * sizeof(typename Types<DT>::T), 128);
+template <int DT> __host__ __device__ constexpr size_t smem_bytes(int slice_words, bool stream) {
+  return smem_slice<DT>(slice_words, stream) +
+         (stream ? size_t(RING_STAGES) * RING_CHUNK
+                 : align_up(size_t(slice_words) * 32 * sizeof(typename Types<DT>::T), 128));
 }
 
 // The last request whose segment starts at or before `row` (empty segments
@@ -207,22 +210,31 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
   using W = typename K::W;
   extern __shared__ __align__(128) uint8_t raw[];
   Smem<W>& s = *reinterpret_cast<Smem<W>*>(raw);
+  const bool stream = p.stream_rows != 0;
   uint32_t* mask_s = reinterpret_cast<uint32_t*>(raw + smem_head<DT>());
-  W* tmax = reinterpret_cast<W*>(raw + smem_tmax<DT>(p.slice_words));
-  T* slice = reinterpret_cast<T*>(raw + smem_slice<DT>(p.slice_words));
+  W* tmax = reinterpret_cast<W*>(raw + smem_tmax<DT>(p.slice_words, stream));
+  T* slice = reinterpret_cast<T*>(raw + smem_slice<DT>(p.slice_words, stream));
   R r(p, s, mask_s, tmax, slice);
   ES_TRACE(p.workspace, p.rows, r.row, r.rank, 0);
 
   // 1. Start copying this rank's slice (and mask words) before waiting for
   //    the preparation kernel: they are inputs, which it never writes.
+  //    Resident rows copy the whole slice; streamed rows fill the TMA ring.
   if (threadIdx.x == 0) {
     mbar_init(&s.bar, 1);
+    for (int i = 0; i < RING_STAGES; ++i) mbar_init(&s.ring_bar[i], 1);
     mbar_init_fence();
   }
   __syncthreads();
   const T* src = static_cast<const T*>(p.target) + int64_t(r.row) * p.t_s0;
   const int n = r.hi - r.lo;
-  if (p.vector_load) {
+  if (stream) {
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(&s.bar, 0);
+      if (p.vector_load)
+        for (int c = 0; c < min(RING_STAGES, r.ring_chunks()); ++c) r.ring_issue(c);
+    }
+  } else if (p.vector_load) {
     const uint32_t bytes = uint32_t(n) * uint32_t(sizeof(T)), bulk = bytes & ~15u;
     if (threadIdx.x == 0) {
       mbar_arrive_expect_tx(&s.bar, bulk);
@@ -235,7 +247,7 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
     if (threadIdx.x == 0) mbar_arrive_expect_tx(&s.bar, 0);
     for (int i = threadIdx.x; i < n; i += THREADS) slice[i] = src[int64_t(r.lo + i) * p.t_s1];
   }
-  if (p.mask != nullptr)
+  if (!stream && p.mask != nullptr)
     for (int w = threadIdx.x; w < (n + 31) / 32; w += THREADS)
       mask_s[w] = uint32_t(p.mask[int64_t(r.row) * p.m_s0 + int64_t(r.lo / 32 + w) * p.m_s1]);
 
@@ -262,7 +274,13 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
     }
   }
   __syncthreads();
-  if (s.ctx.skip) return;  // the same decision on every rank; no rank reads another's memory
+  if (s.ctx.skip) {  // the same decision on every rank; no rank reads another's memory
+    if (stream && p.vector_load && threadIdx.x == 0)  // let the ring copies land before leaving
+      for (int c = 0; c < min(RING_STAGES, r.ring_chunks()); ++c)
+        for (uint32_t spins = 0; !mbar_try_wait(&s.ring_bar[c], 0) && spins < (1u << 22); ++spins) {
+        }
+    return;
+  }
   const RowCtx c = s.ctx;
   const bool draft_row = r.row + 1 < c.end, full_q = draft_row && c.kind == 1;
   const bool verify = draft_row && p.mode == ES_RATIO;
@@ -322,7 +340,7 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
 // Launch of the row kernel: a (C, rows) grid of C-block clusters, with
 // programmatic stream serialization after the preparation kernel.
 template <int DT> cudaError_t launch_rows(const Params& p, int cluster, cudaStream_t stream) {
-  const size_t smem = smem_bytes<DT>(p.slice_words);
+  const size_t smem = smem_bytes<DT>(p.slice_words, p.stream_rows != 0);
   auto kernel = rows_kernel<DT>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;

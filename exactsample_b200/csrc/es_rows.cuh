@@ -64,6 +64,20 @@ __device__ __forceinline__ void load4(const __half* s, float v[4]) {
   v[2] = __half2float(__ushort_as_half(uint16_t(x.y))); v[3] = __half2float(__ushort_as_half(uint16_t(x.y >> 16)));
 }
 
+// Four consecutive values from global memory (16-byte aligned rows).
+__device__ __forceinline__ void load4_global(const float* g, float v[4]) {
+  const float4 x = __ldg(reinterpret_cast<const float4*>(g));
+  v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+}
+__device__ __forceinline__ void load4_global(const double* g, double v[4]) {
+  const double2 x = __ldg(reinterpret_cast<const double2*>(g)), y = __ldg(reinterpret_cast<const double2*>(g) + 1);
+  v[0] = x.x; v[1] = x.y; v[2] = y.x; v[3] = y.y;
+}
+template <class H> __device__ __forceinline__ void load4_global(const H* g, float v[4]) {
+  const uint2 x = __ldg(reinterpret_cast<const uint2*>(g));
+  load4(reinterpret_cast<const H*>(&x), v);
+}
+
 // An exact cut of the order (value desc, token ID asc): keeps the tokens at or
 // before (key, id). `on == 0` keeps everything.
 template <class Key> struct Cut {
@@ -103,6 +117,7 @@ constexpr int TILE_CAP = 256;
 
 template <class W> struct Smem {
   uint64_t bar;
+  uint64_t ring_bar[RING_STAGES];
   int32_t timeout;
   RowCtx ctx;
   // Published to the other ranks, double-buffered by exchange parity.
@@ -187,9 +202,12 @@ template <int DT> struct Row {
 
   const Params& p;
   Smem<W>& s;
-  uint32_t* mask_s;  // this rank's mask words
+  uint32_t* mask_s;  // this rank's mask words (resident rows)
   W* tmax;           // per 32-token tile of the slice: the largest valid value (-inf if none)
-  T* slice;          // this rank's logits
+  T* slice;          // this rank's logits (resident rows) or the TMA ring (streamed rows)
+  const T* grow;     // the slice in global memory
+  int64_t gs;        // its element stride
+  bool resident, vec;
   cg::cluster_group cluster;
   int rank, ranks, row, lo, hi, groups;
   int xc;  // exchanges so far (the same on every rank)
@@ -212,21 +230,45 @@ template <int DT> struct Row {
     groups = (hi - lo + 3) / 4;
     xc = 0;
     has_mask = p.mask != nullptr;
+    resident = !p.stream_rows;
+    vec = p.vector_load != 0;
+    gs = p.t_s1;
+    grow = static_cast<const T*>(p.target) + int64_t(row) * p.t_s0 + int64_t(lo) * p.t_s1;
   }
 
   // ---- slice access ----
   // Mask bits of local group g (tokens allowed and inside the slice).
   __device__ __forceinline__ unsigned group_bits(int g) const {
     const int t = 4 * g;
-    unsigned bits = has_mask ? (mask_s[t >> 5] >> (t & 31)) & 0xfu : 0xfu;
+    unsigned bits = 0xfu;
+    if (has_mask) {
+      const uint32_t word = resident ? mask_s[t >> 5]
+                                     : uint32_t(__ldg(p.mask + int64_t(row) * p.m_s0 + int64_t((lo + t) >> 5) * p.m_s1));
+      bits = (word >> (t & 31)) & 0xfu;
+    }
     const int left = hi - lo - t;
     if (left < 4) bits &= (1u << max(left, 0)) - 1u;
     return bits;
   }
+  // The four values of local group g: shared memory for resident rows,
+  // global memory (L2) otherwise; -inf past the slice.
+  __device__ __forceinline__ void values(int g, W v[4]) const {
+    if (resident) {
+      load4(slice + 4 * g, v);
+    } else if (vec && 4 * g + 4 <= hi - lo) {
+      load4_global(grow + 4 * g, v);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int t = 4 * g + j;
+        v[j] = t < hi - lo ? widen(grow[int64_t(t) * gs]) : W(-INFINITY);
+      }
+    }
+  }
   // Values of local group g and the bits of its valid tokens (allowed, inside
   // the slice, above -inf).
   __device__ __forceinline__ unsigned group(int g, W v[4]) const {
-    load4(slice + 4 * g, v);
+    values(g, v);
     unsigned bits = group_bits(g);
 #pragma unroll
     for (int j = 0; j < 4; ++j)
@@ -317,30 +359,34 @@ template <int DT> struct Row {
     __syncthreads();
     return m;
   }
-  // NaN / +inf anywhere in the slice (even masked), the count of valid
-  // tokens, the maximum with the lowest ID among equals, each 32-token tile's
-  // maximum, and for a full-q draft row the same checks of the proposal row.
-  // Warp-uniform loop: the 8 lanes of a tile combine its maximum by shuffles.
-  __device__ void stats_pass(bool full_q, bool timed_out) {
-    W best = W(-INFINITY), qmax = W(-INFINITY);
-    int best_i = INT_MAX, nvalid = 0, bad = 0, qvalid = 0, qbad = 0;
-    for (int base = warp_id() * 32; base < groups; base += THREADS) {
+  // Statistics accumulated over groups.
+  struct Acc {
+    W best;
+    int best_i, valid, bad;
+  };
+  // Groups [g_begin, g_end) of the slice (g_begin a multiple of 8; every
+  // tile either wholly inside or the slice's last): NaN / +inf anywhere
+  // (even masked), valid count, the maximum with the lowest ID among equals,
+  // and each 32-token tile's maximum. Warp-uniform: the 8 lanes of a tile
+  // combine its maximum by shuffles.
+  template <class Load> __device__ __forceinline__ void stats_groups(int g_begin, int g_end, Load load, Acc& a) {
+    for (int base = g_begin + warp_id() * 32; base < g_end; base += THREADS) {
       const int g = base + lane_id();
       W tile = W(-INFINITY);
-      if (g < groups) {
+      if (g < g_end) {
         W v[4];
-        load4(slice + 4 * g, v);
+        load(g, v);
         const unsigned bits = group_bits(g);
         const int inside = min(4, hi - lo - 4 * g);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          if (j < inside) bad |= !(v[j] < W(INFINITY)) & (v[j] != W(-INFINITY));  // NaN or +inf
+          if (j < inside) a.bad |= !(v[j] < W(INFINITY)) & (v[j] != W(-INFINITY));  // NaN or +inf
           const bool ok = ((bits >> j) & 1u) && v[j] > W(-INFINITY);
           const W x = ok ? v[j] : W(-INFINITY);
-          nvalid += ok;
-          if (x > best) {  // IDs rise within a thread, so ties keep the lowest
-            best = x;
-            best_i = lo + 4 * g + j;
+          a.valid += ok;
+          if (x > a.best) {  // IDs rise within a thread, so ties keep the lowest
+            a.best = x;
+            a.best_i = lo + 4 * g + j;
           }
           tile = x > tile ? x : tile;
         }
@@ -350,8 +396,51 @@ template <int DT> struct Row {
         const W other = shfl_xor(tile, o);
         tile = other > tile ? other : tile;
       }
-      if ((lane_id() & 7) == 0 && g < groups) tmax[g >> 3] = tile;
+      if ((lane_id() & 7) == 0 && g < g_end) tmax[g >> 3] = tile;
     }
+  }
+  // Bytes of the slice the TMA ring carries (whole 16-byte units), in chunks.
+  __device__ __forceinline__ uint32_t ring_bytes() const { return (uint32_t(hi - lo) * uint32_t(sizeof(T))) & ~15u; }
+  __device__ __forceinline__ int ring_chunks() const { return int((ring_bytes() + RING_CHUNK - 1) / RING_CHUNK); }
+  // Thread 0 starts the TMA copy of chunk c into its ring stage.
+  __device__ __forceinline__ void ring_issue(int c) {
+    const uint32_t off = uint32_t(c) * RING_CHUNK, len = min(RING_CHUNK, ring_bytes() - off);
+    uint64_t* bar = &s.ring_bar[c % RING_STAGES];
+    mbar_arrive_expect_tx(bar, len);
+    bulk_load(reinterpret_cast<uint8_t*>(slice) + (c % RING_STAGES) * RING_CHUNK,
+              reinterpret_cast<const uint8_t*>(grow) + off, len, bar);
+  }
+  // The statistics pass over the whole slice: from shared memory (resident),
+  // through the TMA ring (streamed, 16-byte aligned rows), or from global
+  // memory; then the cluster merge. Returns false if a copy never arrived.
+  __device__ bool stats_pass(bool full_q, bool timed_out) {
+    Acc a{W(-INFINITY), INT_MAX, 0, 0};
+    bool lost = timed_out;
+    if (resident) {
+      stats_groups(0, groups, [&](int g, W v[4]) { load4(slice + 4 * g, v); }, a);
+    } else if (vec) {
+      constexpr int GPC = int(RING_CHUNK / (4 * sizeof(T)));  // groups per chunk
+      const int ring_groups = int(ring_bytes() / (4 * sizeof(T))) & ~7;  // whole tiles
+      const int chunks = ring_chunks();
+      for (int c = 0; c < chunks; ++c) {
+        uint32_t spins = 0;
+        while (!mbar_try_wait(&s.ring_bar[c % RING_STAGES], uint32_t(c / RING_STAGES) & 1u))
+          if (++spins >= (1u << 22)) {
+            lost = true;
+            break;
+          }
+        const T* stage = slice + (c % RING_STAGES) * (RING_CHUNK / sizeof(T)) - int64_t(c) * GPC * 4;
+        stats_groups(c * GPC, min((c + 1) * GPC, ring_groups),
+                     [&](int g, W v[4]) { load4(stage + 4 * g, v); }, a);
+        __syncthreads();  // every thread is done with this stage
+        if (threadIdx.x == 0 && c + RING_STAGES < chunks) ring_issue(c + RING_STAGES);
+      }
+      stats_groups(ring_groups, groups, [&](int g, W v[4]) { values(g, v); }, a);  // the last partial tile
+    } else {
+      stats_groups(0, groups, [&](int g, W v[4]) { values(g, v); }, a);
+    }
+    W qmax = W(-INFINITY);
+    int qvalid = 0, qbad = 0;
     if (full_q)
       for (int t = lo + int(threadIdx.x); t < hi; t += THREADS) {
         const W y = q_value(t);
@@ -359,8 +448,9 @@ template <int DT> struct Row {
         qvalid += y > W(-INFINITY);
         qmax = y > qmax ? y : qmax;
       }
-    if (timed_out) bad = 1;  // this rank's slice never arrived: the row is not trusted
-    const Stats<W> merged = block_stats(Stats<W>{best, qmax, best_i, nvalid, bad, qvalid, qbad});
+    lost = __syncthreads_or(lost);
+    if (lost) a.bad = 1;  // a slice copy never arrived: the row is not trusted
+    const Stats<W> merged = block_stats(Stats<W>{a.best, qmax, a.best_i, a.valid, a.bad, qvalid, qbad});
     if (threadIdx.x == 0) s.stats[parity()] = merged;
     ES_TRACE(p.workspace, p.rows, row, rank, 8);
     exchange();
@@ -371,6 +461,7 @@ template <int DT> struct Row {
     for (int r = 1; r < ranks; ++r) all = merge_stats(all, s.peers.stats[r]);
     maxv = all.b1v;
     __syncthreads();
+    return !lost;
   }
 
   // ---- cluster-wide reductions ----

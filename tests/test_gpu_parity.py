@@ -277,3 +277,20 @@ def test_results_do_not_depend_on_the_cluster_split(ranks, monkeypatch):
                         context=f"{name} ranks={ranks}")
     for case, expected in SMALL[::7]:
         assert_same(run_abi(device_inputs(case), mode=case["mode"], list_max=0), expected, context=case["name"])
+
+
+@pytest.mark.parametrize("stream", ["0", "1"])
+def test_results_do_not_depend_on_the_row_mode(stream, monkeypatch):
+    """Resident rows (slices kept in shared memory) and streamed rows (TMA ring,
+    later passes from L2) give identical results."""
+    monkeypatch.setenv("EXACTSAMPLE_STREAM", stream)
+    for entry in _large():
+        name, subset, digest, expected = entry
+        case = golden_io.large_case(name, subset, digest)
+        for list_max in [256, 0]:
+            assert_same(run_abi(device_inputs(case), mode=case["mode"], list_max=list_max), expected,
+                        context=f"{name} stream={stream}")
+    for case, expected in SMALL[::3]:
+        for list_max in [256, 0]:
+            assert_same(run_abi(device_inputs(case), mode=case["mode"], list_max=list_max), expected,
+                        context=case["name"])
