@@ -46,7 +46,7 @@ template <int DT> struct RowKernel {
 
   // Target point mass at the greedy token (temperature 0).
   __device__ static void greedy(R& r, const RowCtx& c, bool verify, bool full_q, double sq, RowResult& res) {
-    const int g = r.greedy_id();
+    const int g = r.all.b1i;
     res.sample = g;
     if (!verify) return;
     res.accept = c.draft_id == g;
@@ -66,98 +66,6 @@ template <int DT> struct RowKernel {
     if (!full_q) return 1.0;
     const W y = r.q_value(c.draft_id);
     return y > W(-INFINITY) ? exp(double(y) - double(r.all.qmax)) / sq : 0.0;
-  }
-
-  // Rank 0's warp 0 finishes a list row of at most 32 candidates in
-  // registers: the same steps as list_finish (sort, FP64 weights, min-p,
-  // exact top-p prefix, normalization, draws, ratio test), with warp
-  // shuffles and no block barriers.
-  __device__ static void list_finish_warp(R& r, const RowCtx& c, int m, int n_keep, bool verify, bool full_q,
-                                          double sq, double u_accept, RowResult& res) {
-    auto& s = r.s;
-    const int i = lane_id();
-    uint64_t key = i < m ? s.u.cand.key[i] : 0;
-    int id = i < m ? s.u.cand.id[i] : INT_MAX;
-    // Bitonic sort into (key desc, ID asc) order across the 32 lanes.
-#pragma unroll
-    for (int kk = 2; kk <= 32; kk <<= 1)
-#pragma unroll
-      for (int j = kk >> 1; j > 0; j >>= 1) {
-        const uint64_t ok = __shfl_xor_sync(0xffffffffu, key, j);
-        const int oid = __shfl_xor_sync(0xffffffffu, id, j);
-        const bool mine_first = key > ok || (key == ok && id < oid);
-        const bool lower = (i & j) == 0, desc = (i & kk) == 0;
-        if (mine_first != (lower == desc)) {
-          key = ok;
-          id = oid;
-        }
-      }
-    const bool in = i < n_keep;
-    double w = 0;
-    bool ok = false;
-    if (in) {
-      w = exp(r.x64(key_value(Key(key))));
-      ok = w >= r.min_p && w > 0;
-    }
-    const unsigned out = __ballot_sync(0xffffffffu, in && !ok);
-    const int n1 = out ? min(n_keep, __ffs(out) - 1) : n_keep;
-    u128 prefix = i < n1 ? fx_of(w) : u128(0);
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const u128 y = (u128(__shfl_up_sync(0xffffffffu, uint64_t(prefix >> 64), o)) << 64) |
-                     __shfl_up_sync(0xffffffffu, uint64_t(prefix), o);
-      if (i >= o) prefix += y;
-    }
-    auto at_lane = [&](u128 v, int lane) {
-      return (u128(__shfl_sync(0xffffffffu, uint64_t(v >> 64), lane)) << 64) |
-             __shfl_sync(0xffffffffu, uint64_t(v), lane);
-    };
-    bool near;
-    const double d1 = fx_round(at_lane(prefix, n1 - 1), uint32_t(n1), &near);
-    r.count_near_tie(near);
-    int n2 = n1;
-    double denominator = d1;
-    if (r.top_p < 1) {
-      const double target = r.top_p * d1;
-      if (target <= 1.0) {
-        n2 = 1;  // the first token's weight is exactly 1
-      } else {
-        bool nr = false;
-        const unsigned reach = __ballot_sync(0xffffffffu, i < n1 && fx_reaches(prefix, uint32_t(i + 1), target, &nr));
-        n2 = reach ? __ffs(reach) : n1;
-      }
-      denominator = fx_round(at_lane(prefix, n2 - 1), uint32_t(n2), &near);
-      r.count_near_tie(near);
-    }
-    const double prob = i < n2 ? w / denominator : 0.0;
-    auto draw_list = [&](uint32_t sub, int excluded) {
-      Best b = no_best();
-      if (i < n2 && id != excluded && prob > 0) b = Best{log(prob) + noise64(r.addr.word(sub, uint32_t(id))), id};
-      b = warp_all(b, [](Best a, Best c2) { return best_of(a, c2); });
-      return b.id == INT_MAX ? -1 : b.id;
-    };
-    if (!verify) {
-      res.sample = draw_list(0, -1);
-      return;
-    }
-    const unsigned hit = __ballot_sync(0xffffffffu, i < n2 && id == c.draft_id);
-    const double px = hit ? __shfl_sync(0xffffffffu, prob, __ffs(hit) - 1) : 0.0;
-    const double qx = q_of_draft(r, c, full_q, sq);
-    res.accept = u_accept < fmin(1.0, px / qx);
-    if (res.accept) return;
-    if (!full_q) {
-      res.residual = draw_list(2, c.draft_id);
-      return;
-    }
-    Best b = no_best();
-    if (i < n2 && prob > 0) {
-      const W y = r.q_value(id);
-      const double q = y > W(-INFINITY) ? exp(double(y) - double(r.all.qmax)) / sq : 0.0;
-      const double rr = fmax(prob - q, 0.0);
-      if (rr > 0) b = Best{log(rr) + noise64(r.addr.word(2, uint32_t(id))), id};
-    }
-    b = warp_all(b, [](Best a, Best c2) { return best_of(a, c2); });
-    res.residual = b.id == INT_MAX ? -1 : b.id;
   }
 
   // Rank 0 finishes a list row: the m gathered candidates hold the kept
@@ -262,13 +170,7 @@ template <int DT> struct RowKernel {
       } else {
         m = r.gather_all([](W, int) { return true; });
       }
-      if (r.rank == 0) {
-        if (m <= 32) {
-          if (warp_id() == 0) list_finish_warp(r, c, m, n_keep, verify, full_q, sq, u_accept, res);
-        } else {
-          list_finish(r, c, m, n_keep, verify, full_q, sq, u_accept, res);
-        }
-      }
+      if (r.rank == 0) list_finish(r, c, m, n_keep, verify, full_q, sq, u_accept, res);
       return true;
     }
     Cut<Key> cut_k{0, 0, 0}, cut_p{0, 0, 0};

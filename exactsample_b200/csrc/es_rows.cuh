@@ -96,12 +96,9 @@ constexpr float SCORE_ERR = 1.5e-6f;
 // Tokens are pruned only this far below the best lower bound so far, so a
 // pruned bound rarely blocks the certificate of a different winner.
 constexpr float PRUNE_MARGIN = 1e-3f;
-// Widths below the row maximum (logits) tried for list candidates: 0.5 to
-// 64 in steps of sqrt 2.
-constexpr int NEAR_WINDOWS = 15;
-__device__ __forceinline__ float near_width(int i) {
-  return (i & 1 ? 0.70710678f : 0.5f) * float(1 << (i >> 1));
-}
+// Distance windows (logits below the maximum) tried for list candidates.
+constexpr int WINDOWS = 8;
+__device__ __forceinline__ float window_width(int i) { return 0.25f * float(1 << i); }  // 0.25 .. 32
 
 // exp((v - max) / T) >= min_p and > 0 in FP64, for the rare token whose
 // FP32 value is too close to a threshold (out of line: keeps the loops lean).
@@ -126,7 +123,7 @@ template <class W> struct Smem {
   // Published to the other ranks, double-buffered by exchange parity.
   Stats<W> stats[2];
   uint32_t hist[2][RADIX];
-  int32_t wcount[2][NEAR_WINDOWS];
+  int32_t wcount[2][WINDOWS];
   u128 fx[2];
   uint32_t fxn[2];
   Pick pick[2];
@@ -139,8 +136,7 @@ template <class W> struct Smem {
     u128 fxs[WARPS];
     int32_t ints[WARPS];
     uint32_t uints[WARPS];
-    int32_t near[WARPS][NEAR_WINDOWS];
-    W ws[WARPS];
+    int32_t win[WARPS][WINDOWS];
     Stats<W> stats[WARPS];
   } red;
   // Peers' published slots, copied here by a few threads after an exchange.
@@ -149,7 +145,7 @@ template <class W> struct Smem {
     Pick picks[16];
     Best bests[16];
     u128 fx[16];
-    int32_t ints[16 * NEAR_WINDOWS + 16];
+    int32_t ints[16 * WINDOWS + 16];
   } peers;
   uint32_t peer_n[16];
   int32_t pushed[16];  // per-rank counts each rank writes into every rank's copy
@@ -363,19 +359,16 @@ template <int DT> struct Row {
     __syncthreads();
     return m;
   }
-  // Statistics accumulated over groups (the argmax is found later, only
-  // where a row needs it, from the tile maxima).
+  // Statistics accumulated over groups.
   struct Acc {
     W best;
-    int valid, bad;
+    int best_i, valid, bad;
   };
   // Groups [g_begin, g_end) of the slice (g_begin a multiple of 8; every
   // tile either wholly inside or the slice's last): NaN / +inf anywhere
-  // (even masked), the valid count, the maximum, and each 32-token tile's
-  // maximum. Warp-uniform: the 8 lanes of a tile combine its maximum by
-  // shuffles. A full unmasked group costs about six instructions per token:
-  // a quarter-scaled sum is NaN or +inf iff a value is (scaling keeps finite
-  // sums finite), and -inf values are counted only when the sum shows one.
+  // (even masked), valid count, the maximum with the lowest ID among equals,
+  // and each 32-token tile's maximum. Warp-uniform: the 8 lanes of a tile
+  // combine its maximum by shuffles.
   template <class Load> __device__ __forceinline__ void stats_groups(int g_begin, int g_end, Load load, Acc& a) {
     for (int base = g_begin + warp_id() * 32; base < g_end; base += THREADS) {
       const int g = base + lane_id();
@@ -383,28 +376,20 @@ template <int DT> struct Row {
       if (g < g_end) {
         W v[4];
         load(g, v);
-        const int inside = hi - lo - 4 * g;
-        if (!has_mask && inside >= 4) {
-          const W q = (v[0] * W(0.25) + v[1] * W(0.25)) + (v[2] * W(0.25) + v[3] * W(0.25));
-          a.bad |= !(q < W(INFINITY)) & (q != W(-INFINITY));
-          int n = 4;
-          if (q == W(-INFINITY)) n -= (v[0] == W(-INFINITY)) + (v[1] == W(-INFINITY)) + (v[2] == W(-INFINITY)) +
-                                      (v[3] == W(-INFINITY));
-          a.valid += n;
-          const W m01 = v[0] > v[1] ? v[0] : v[1], m23 = v[2] > v[3] ? v[2] : v[3];
-          tile = m01 > m23 ? m01 : m23;
-        } else {
-          const unsigned bits = group_bits(g);
+        const unsigned bits = group_bits(g);
+        const int inside = min(4, hi - lo - 4 * g);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if (j < inside) a.bad |= !(v[j] < W(INFINITY)) & (v[j] != W(-INFINITY));  // NaN or +inf
-            const bool ok = ((bits >> j) & 1u) && v[j] > W(-INFINITY);
-            a.valid += ok;
-            const W x = ok ? v[j] : W(-INFINITY);
-            tile = x > tile ? x : tile;
+        for (int j = 0; j < 4; ++j) {
+          if (j < inside) a.bad |= !(v[j] < W(INFINITY)) & (v[j] != W(-INFINITY));  // NaN or +inf
+          const bool ok = ((bits >> j) & 1u) && v[j] > W(-INFINITY);
+          const W x = ok ? v[j] : W(-INFINITY);
+          a.valid += ok;
+          if (x > a.best) {  // IDs rise within a thread, so ties keep the lowest
+            a.best = x;
+            a.best_i = lo + 4 * g + j;
           }
+          tile = x > tile ? x : tile;
         }
-        a.best = tile > a.best ? tile : a.best;
       }
 #pragma unroll
       for (int o = 1; o < 8; o <<= 1) {
@@ -414,30 +399,6 @@ template <int DT> struct Row {
       if ((lane_id() & 7) == 0 && g < g_end) tmax[g >> 3] = tile;
     }
   }
-  __device__ __forceinline__ int n_tiles() const { return (groups + 7) / 8; }
-  // The lowest-ID valid token of this rank's slice whose value is `target`
-  // (INT_MAX if none): only tiles whose maximum is at least `target` are read.
-  __device__ int first_at_value(W target) {
-    int found = INT_MAX;
-    for (int t = threadIdx.x; t < n_tiles(); t += THREADS) {
-      if (!(tmax[t] >= target)) continue;
-      for (int gg = 0; gg < 8 && found == INT_MAX; ++gg) {
-        const int g = t * 8 + gg;
-        if (g >= groups) break;
-        W v[4];
-        const unsigned bits = group(g, v);
-        for (int j = 0; j < 4; ++j)
-          if (((bits >> j) & 1u) && v[j] == target) {
-            found = lo + 4 * g + j;
-            break;
-          }
-      }
-    }
-    return block_all(found, [](int x, int y) { return x < y ? x : y; }, s.red.ints);
-  }
-  // The row's greedy token: the lowest ID with the maximum (over the cluster).
-  __device__ int greedy_id() { return cluster_min(first_at_value(maxv)); }
-
   // Bytes of the slice the TMA ring carries (whole 16-byte units), in chunks.
   __device__ __forceinline__ uint32_t ring_bytes() const { return (uint32_t(hi - lo) * uint32_t(sizeof(T))) & ~15u; }
   __device__ __forceinline__ int ring_chunks() const { return int((ring_bytes() + RING_CHUNK - 1) / RING_CHUNK); }
@@ -453,7 +414,7 @@ template <int DT> struct Row {
   // through the TMA ring (streamed, 16-byte aligned rows), or from global
   // memory; then the cluster merge. Returns false if a copy never arrived.
   __device__ bool stats_pass(bool full_q, bool timed_out) {
-    Acc a{W(-INFINITY), 0, 0};
+    Acc a{W(-INFINITY), INT_MAX, 0, 0};
     bool lost = timed_out;
     if (resident) {
       stats_groups(0, groups, [&](int g, W v[4]) { load4(slice + 4 * g, v); }, a);
@@ -489,7 +450,7 @@ template <int DT> struct Row {
       }
     lost = __syncthreads_or(lost);
     if (lost) a.bad = 1;  // a slice copy never arrived: the row is not trusted
-    const Stats<W> merged = block_stats(Stats<W>{a.best, qmax, INT_MAX, a.valid, a.bad, qvalid, qbad});
+    const Stats<W> merged = block_stats(Stats<W>{a.best, qmax, a.best_i, a.valid, a.bad, qvalid, qbad});
     if (threadIdx.x == 0) s.stats[parity()] = merged;
     ES_TRACE(p.workspace, p.rows, row, rank, 8);
     exchange();
@@ -697,69 +658,58 @@ template <int DT> struct Row {
     return d < float(DIST_BINS / 2) ? int(d * 2.f) : DIST_BINS;
   }
   // The top-n valid tokens (and every token tied with the n-th) gathered to
-  // rank 0. Each rank counts its 32-token tiles whose maximum lies within
-  // each of NEAR_WINDOWS widths below the row maximum (0.5 to 64 logits,
-  // spaced by sqrt 2; registers only, one pass over the tile maxima). Every
-  // such tile holds a token within the width, so the narrowest width whose
-  // tile count reaches n holds at least n tokens: those are gathered, from
-  // the tiles within it only. Slots in rank 0's buffer come from an atomic
-  // counter there; each rank pushes its count to every rank before the
-  // closing exchange. Returns the count, or -1 if no width qualifies or the
-  // tokens do not fit the buffer (the caller then radix-selects).
+  // rank 0. The ranks histogram their 32-token tiles by the distance of each
+  // tile's maximum below the row's; the first bin b where the cumulative tile
+  // count reaches n bounds the n-th token (every such tile has a token within
+  // bin b), so every valid token with bin <= b is gathered, from those tiles
+  // only. Slots in rank 0's buffer come from an atomic counter there; each
+  // rank pushes its count to every rank before the closing exchange. Returns
+  // the count, or -1 if no bin below 64 logits qualifies or the tokens do not
+  // fit the buffer (the caller then radix-selects).
   __device__ int gather_near(int n) {
-    int c[NEAR_WINDOWS] = {};
-    for (int t = threadIdx.x; t < n_tiles(); t += THREADS) {
-      const float d = float(maxv - tmax[t]);  // +inf for a tile without valid tokens
-#pragma unroll
-      for (int i = 0; i < NEAR_WINDOWS; ++i) c[i] += d <= near_width(i);
-    }
-#pragma unroll
-    for (int i = 0; i < NEAR_WINDOWS; ++i) c[i] = warp_all(c[i], [](int x, int y) { return x + y; });
-    if (lane_id() == 0)
-      for (int i = 0; i < NEAR_WINDOWS; ++i) s.red.near[warp_id()][i] = c[i];
+    uint32_t* h = s.hist[parity()];
+    for (int i = threadIdx.x; i < RADIX; i += THREADS) h[i] = 0;
     if (threadIdx.x == 0) s.n_cand = 0;
     __syncthreads();
-    if (threadIdx.x < NEAR_WINDOWS) {
-      int t = 0;
-      for (int w = 0; w < WARPS; ++w) t += s.red.near[w][threadIdx.x];
-      s.wcount[parity()][threadIdx.x] = t;
+    const int n_tiles = (groups + 7) / 8;
+    for (int base = warp_id() * 32; base < n_tiles; base += THREADS) {
+      const int t = base + lane_id();
+      const int b = t < n_tiles && tmax[t] > W(-INFINITY) ? min(dist_bin(tmax[t]), DIST_BINS) : -1;
+      warp_bucket_add(nullptr, h, b, 0);
     }
     exchange();
-    if (int(threadIdx.x) < ranks * NEAR_WINDOWS)
-      s.peers.ints[threadIdx.x] = peer(s.wcount[parity() ^ 1], threadIdx.x / NEAR_WINDOWS)[threadIdx.x % NEAR_WINDOWS];
+    int cnt = 0;
+    if (int(threadIdx.x) < DIST_BINS)
+      for (int rr = 0; rr < ranks; ++rr) cnt += int(peer(s.hist[parity() ^ 1], rr)[threadIdx.x]);
+    int total;
+    const int cum = block_scan(cnt, s.red.ints, &total);
+    if (threadIdx.x == 0) s.ival[0] = -1;
     __syncthreads();
-    int pick = -1;
-    for (int i = 0; i < NEAR_WINDOWS && pick < 0; ++i) {
-      int t = 0;
-      for (int rr = 0; rr < ranks; ++rr) t += s.peers.ints[rr * NEAR_WINDOWS + i];
-      if (t >= n) pick = i;
-    }
+    if (cum >= n && cum - cnt < n) s.ival[0] = threadIdx.x;
     __syncthreads();
+    const int window = s.ival[0];
     ES_TRACE(p.workspace, p.rows, row, rank, 4);
-    if (pick < 0) return -1;
-    const float width = near_width(pick);
+    if (window < 0) return -1;
     int* counter = peer(&s.n_cand, 0);
     uint64_t* keys = peer(s.u.cand.key, 0);
     int32_t* ids = peer(s.u.cand.id, 0);
     int mine = 0;
-    for (int t = threadIdx.x; t < n_tiles(); t += THREADS) {
-      if (!(float(maxv - tmax[t]) <= width)) continue;  // the tile's maximum is farther: so are its tokens
-      for (int g = t * 8; g < min(t * 8 + 8, groups); ++g) {
-        W v[4];
-        const unsigned bits = group(g, v);
+    for (int g = threadIdx.x; g < groups; g += THREADS) {
+      if (dist_bin(tmax[g >> 3]) > window) continue;  // the tile's maximum is farther: so are its tokens
+      W v[4];
+      const unsigned bits = group(g, v);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if (!((bits >> j) & 1u) || !(float(maxv - v[j]) <= width)) continue;
-          ++mine;
-          const int at_ = atomicAdd(counter, 1);
-          if (at_ < CAP) {
-            keys[at_] = uint64_t(order_key(v[j]));
-            ids[at_] = lo + 4 * g + j;
-          }
+      for (int j = 0; j < 4; ++j) {
+        if (!((bits >> j) & 1u) || dist_bin(v[j]) > window) continue;
+        ++mine;
+        const int at_ = atomicAdd(counter, 1);
+        if (at_ < CAP) {
+          keys[at_] = uint64_t(order_key(v[j]));
+          ids[at_] = lo + 4 * g + j;
         }
       }
     }
-    mine = block_all(mine, [](int x, int y) { return x + y; }, s.red.ints);
+    mine = block_all(mine, [](int a, int b) { return a + b; }, s.red.ints);
     if (int(threadIdx.x) < ranks) peer(s.pushed, threadIdx.x)[rank] = mine;
     exchange();
     int gathered = 0;
@@ -902,7 +852,7 @@ template <int DT> struct Row {
         if (target <= 1.0) {
           // The first kept token (the maximum, weight exactly 1) reaches it.
           *normalizer = 1.0;
-          return Cut<Key>{1, order_key(maxv), greedy_id()};
+          return Cut<Key>{1, order_key(maxv), all.b1i};
         }
       }
       bool near = false;
@@ -963,15 +913,11 @@ template <int DT> struct Row {
   // whose bound reaches the FP32 winner's lower bound when the certificate
   // fails (or of every token, with exact_only). Returns -1 if none is kept.
   template <class Kept> __device__ int draw(uint32_t sub, int excluded, Kept kept, bool exact_only) {
-    // A kept token's score bounds the winner's from below: this rank's own
-    // largest token (the row maximum's score is the usual winner).
-    W local_max = W(-INFINITY);
-    for (int t = threadIdx.x; t < n_tiles(); t += THREADS) local_max = tmax[t] > local_max ? tmax[t] : local_max;
-    local_max = block_all(local_max, [](W x, W y) { return x > y ? x : y; }, s.red.ws);
-    const int floor_token = local_max > W(-INFINITY) ? first_at_value(local_max) : INT_MAX;
     if (threadIdx.x == 0) {
+      // A kept token's score bounds the winner's from below: the maximum
+      // (x = 0), or the runner-up when the maximum is excluded.
       float floor = -INFINITY;
-      const int t = floor_token != excluded ? floor_token : INT_MAX;
+      const int t = all.b1i != excluded ? all.b1i : INT_MAX;
       if (t != INT_MAX && valid_global(t)) {
         const W v = value_global(t);
         const float x = x32(v);
