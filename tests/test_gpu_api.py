@@ -34,11 +34,16 @@ def test_workspace_conflict_and_separate_plans():
     from exactsample_b200.cuda import verify
     args = prepared(np.zeros((1, 4)), [0, 1], np.empty((1, 0)))
     other = prepared(np.zeros((1, 4)), [0, 1], np.empty((1, 0)))
+    # A first call loads the kernels (lazily, possibly for longer than the
+    # sleep below); after it the first stream's call is still queued behind
+    # the sleep when the second stream tries the same workspace.
+    verify(**other)
+    other["plan"].synchronize()
     first, second = torch.cuda.Stream(), torch.cuda.Stream()
     first.wait_stream(torch.cuda.current_stream())
     second.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(first):
-        torch.cuda._sleep(100_000_000)
+        torch.cuda._sleep(1_000_000_000)  # about half a second
         verify(**args)
     with torch.cuda.stream(second):
         with pytest.raises(RuntimeError, match="in flight"):
