@@ -15,7 +15,9 @@ ES_F32, ES_F64, ES_F16, ES_BF16, ES_I32, ES_I64, ES_U8 = range(7)
 ERRORS = {0: "ES_SUCCESS", -1: "ES_ERR_ARGUMENT", -2: "ES_ERR_CAPACITY", -3: "ES_ERR_ALIGNMENT",
           -4: "ES_ERR_ALIAS", -5: "ES_ERR_UNSUPPORTED", -6: "ES_ERR_LAUNCH", -7: "ES_ERR_DEVICE"}
 # Every function the header declares.
-EXPORTS = ["es_workspace_bytes", "es_verify", "es_verify_timed", "es_last_error", "es_abi_version"]
+EXPORTS = ["es_workspace_bytes", "es_verify", "es_verify_timed", "es_verify_static", "es_last_error",
+           "es_abi_version"]
+STATIC_MAX_ROWS = 4096  # ES_STATIC_MAX_ROWS
 
 
 class Tensor(ctypes.Structure):
@@ -52,6 +54,8 @@ def load(path: str | Path | None = None) -> ctypes.CDLL:
         lib.es_verify.restype = ctypes.c_int
         lib.es_verify_timed.argtypes = [ctypes.POINTER(Args), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         lib.es_verify_timed.restype = ctypes.c_int
+        lib.es_verify_static.argtypes = [ctypes.POINTER(Args), ctypes.c_void_p]
+        lib.es_verify_static.restype = ctypes.c_int
         lib.es_last_error.argtypes = []
         lib.es_last_error.restype = ctypes.c_char_p
         lib.es_abi_version.argtypes = []
@@ -93,8 +97,9 @@ class AbiError(RuntimeError):
 
 
 def call(tensors: dict, *, mode: int = 0, dispatch: int = 0, max_draft: int = 0, list_max: int = 256,
-         stream=None, events=None) -> None:
-    """es_verify (or es_verify_timed with events=(before, after)) on torch tensors.
+         stream=None, events=None, static_scratch: bool = False) -> None:
+    """es_verify (es_verify_timed with events=(before, after); es_verify_static
+    with static_scratch=True, which ignores any workspace given) on torch tensors.
 
     ``tensors`` maps the es_args field names to torch tensors (optional ones may
     be absent or None). ``stream`` is a torch.cuda.Stream (default: current).
@@ -103,11 +108,14 @@ def call(tensors: dict, *, mode: int = 0, dispatch: int = 0, max_draft: int = 0,
 
     args = Args()
     for name in FIELDS:
-        setattr(args, name, describe(tensors.get(name)))
+        if not (static_scratch and name == "workspace"):
+            setattr(args, name, describe(tensors.get(name)))
     args.mode, args.dispatch, args.max_draft, args.list_max = mode, dispatch, max_draft, list_max
     s = (stream or torch.cuda.current_stream()).cuda_stream
     lib = load()
-    if events is None:
+    if static_scratch:
+        code = lib.es_verify_static(ctypes.byref(args), ctypes.c_void_p(s))
+    elif events is None:
         code = lib.es_verify(ctypes.byref(args), ctypes.c_void_p(s))
     else:
         before, after = events

@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <numeric>
 #include <string>
 
@@ -216,7 +217,12 @@ int device_check() {
   return ES_SUCCESS;
 }
 
-int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaEvent_t after) {
+// `own_scratch`: 0 when the caller provides the workspace (sized by the
+// reference's formula); otherwise the bytes of the library's static scratch
+// that a->workspace describes (es_verify_static), checked against what this
+// call's kernels actually use.
+int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaEvent_t after,
+                uint64_t own_scratch = 0) {
   g_error.clear();
   if (a == nullptr) return fail(ES_ERR_ARGUMENT, "null arguments");
   const es_tensor& logits = a->target_logits;
@@ -269,12 +275,16 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
   if (!(ws.stride[0] == 1 || ws.size[0] <= 1)) return fail(ES_ERR_ARGUMENT, "workspace must be contiguous");
   if (uint64_t(rows) > uint64_t(INT64_MAX - 8) / (sizeof(es::RowResult) + uint64_t(vocab) * 20))
     return fail(ES_ERR_ARGUMENT, "workspace size overflow");
-  uint64_t need = 0;
-  es_workspace_bytes(rows, vocab, a->dispatch == ES_REFERENCE, &need);
-  if (uint64_t(ws.size[0]) < need)
-    return fail(ES_ERR_CAPACITY, a->dispatch == ES_REFERENCE
-                                     ? "workspace capacity exceeded (the reference path needs a plan made with reference=True)"
-                                     : "workspace capacity exceeded");
+  if (own_scratch == 0) {
+    uint64_t need = 0;
+    es_workspace_bytes(rows, vocab, a->dispatch == ES_REFERENCE, &need);
+    if (uint64_t(ws.size[0]) < need)
+      return fail(ES_ERR_CAPACITY, a->dispatch == ES_REFERENCE
+                                       ? "workspace capacity exceeded (the reference path needs a plan made with reference=True)"
+                                       : "workspace capacity exceeded");
+  } else if (es::workspace_needed(rows) > own_scratch) {
+    return fail(ES_ERR_CAPACITY, "target rows exceed the static scratch of es_verify_static");
+  }
   if (reinterpret_cast<uintptr_t>(ws.data) % 8 != 0) return fail(ES_ERR_ALIGNMENT, "workspace alignment must be 8 bytes");
   if (!check(a->tokens, ES_I64, 2, "tokens")) return ES_ERR_ARGUMENT;
   if (!(a->tokens.size[0] >= requests && a->tokens.size[1] >= a->max_draft + 1))
@@ -352,6 +362,41 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
   if (e != cudaSuccess) return fail(ES_ERR_LAUNCH, std::string("exactsample kernel launch failed: ") + cudaGetErrorString(e));
   return ES_SUCCESS;
 }
+
+// ---- es_verify_static: scratch owned by the library ----
+// One scratch area per device, in static device memory, for callers that
+// cannot allocate device memory. It holds the per-call records that a
+// caller-provided workspace would (flags, counters, one result, arrival
+// counter and context record per target row): about 116 bytes per row, so
+// 512 KiB covers ES_STATIC_MAX_ROWS rows.
+constexpr uint64_t STATIC_SCRATCH_BYTES = 512 * 1024;
+constexpr int MAX_DEVICES = 64;
+}  // namespace
+
+static __device__ __align__(256) uint8_t es_static_scratch[STATIC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_scratch_mutex;
+void* g_scratch[MAX_DEVICES] = {};
+
+// The current device's scratch address, looked up on the first call made with
+// that device current (this also loads the library's module on the device).
+int static_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(ES_ERR_DEVICE, "no CUDA device is available");
+  if (dev < 0 || dev >= MAX_DEVICES) return fail(ES_ERR_DEVICE, "device ordinal beyond es_verify_static's table");
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, es_static_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(ES_ERR_DEVICE, std::string("es_verify_static could not find its scratch on this device: ") +
+                                     cudaGetErrorString(e));
+    g_scratch[dev] = p;
+  }
+  *out = g_scratch[dev];
+  return ES_SUCCESS;
+}
 }  // namespace
 
 extern "C" {
@@ -370,6 +415,26 @@ int es_verify(const es_args* args, void* stream) {
 int es_verify_timed(const es_args* args, void* stream, void* before, void* after) {
   return verify_impl(args, static_cast<cudaStream_t>(stream), static_cast<cudaEvent_t>(before),
                      static_cast<cudaEvent_t>(after));
+}
+
+int es_verify_static(const es_args* args, void* stream) {
+  g_error.clear();
+  if (args == nullptr) return fail(ES_ERR_ARGUMENT, "null arguments");
+  if (args->workspace.ndim != 0 || args->workspace.data != nullptr)
+    return fail(ES_ERR_ARGUMENT, "es_verify_static uses its own scratch: leave workspace empty (zeroed)");
+  if (args->target_logits.ndim == 2 && args->target_logits.size[0] > ES_STATIC_MAX_ROWS)
+    return fail(ES_ERR_CAPACITY, "es_verify_static handles at most " + std::to_string(ES_STATIC_MAX_ROWS) +
+                                     " target rows per call (got " + std::to_string(args->target_logits.size[0]) +
+                                     "); use es_verify with a workspace for more");
+  void* scratch = nullptr;
+  if (const int rc = static_scratch(&scratch); rc != ES_SUCCESS) return rc;
+  es_args a = *args;
+  a.workspace.data = scratch;
+  a.workspace.size[0] = int64_t(STATIC_SCRATCH_BYTES);
+  a.workspace.stride[0] = 1;
+  a.workspace.dtype = ES_U8;
+  a.workspace.ndim = 1;
+  return verify_impl(&a, static_cast<cudaStream_t>(stream), nullptr, nullptr, STATIC_SCRATCH_BYTES);
 }
 
 const char* es_last_error(void) { return g_error.c_str(); }

@@ -111,6 +111,32 @@ int es_verify(const es_args* args, void* stream);
  * it exists so that benchmarks can time the dominant kernel by itself. */
 int es_verify_timed(const es_args* args, void* stream, void* before, void* after);
 
+/* es_verify without a caller-provided workspace. No counterpart in the
+ * reference, whose launch always takes the caller's workspace.
+ *
+ * For callers that cannot allocate device memory: for example a sampler
+ * plugin inside a serving engine that reserves all of the GPU's memory up
+ * front and hands its plugins no scratch buffer, or a C host that has no
+ * device allocator of its own. The call allocates nothing (no cudaMalloc or
+ * cudaFree, no allocating library routine): its scratch is a fixed area of
+ * static device memory in this library, one per device, of 512 KiB, enough
+ * for ES_STATIC_MAX_ROWS target rows. A call with more rows returns
+ * ES_ERR_CAPACITY before anything is enqueued. `args->workspace` must be left
+ * empty (zeroed); every other field means what it means for es_verify.
+ *
+ * The first call on a device does the set-up: it looks up that device's
+ * scratch address (cudaGetSymbolAddress, with the device current), which also
+ * loads the library's kernels there. Make that first call before any stream
+ * capture.
+ *
+ * The scratch needs no clearing between calls: each call's first kernel
+ * writes every flag, counter and per-row record that its later kernels read.
+ * But it is one area per device, shared by every call on that device: calls
+ * queued on one stream are ordered, while calls that overlap on different
+ * streams race on the scratch and give wrong results. Serialize them. */
+#define ES_STATIC_MAX_ROWS 4096
+int es_verify_static(const es_args* args, void* stream);
+
 /* The message of the last error returned on this thread ("" after success). */
 const char* es_last_error(void);
 
