@@ -46,7 +46,7 @@ template <int DT> struct RowKernel {
 
   // Target point mass at the greedy token (temperature 0).
   __device__ static void greedy(R& r, const RowCtx& c, bool verify, bool full_q, double sq, RowResult& res) {
-    const int g = r.all.b1i;
+    const int g = r.argmax_id();
     res.sample = g;
     if (!verify) return;
     res.accept = c.draft_id == g;

@@ -108,8 +108,8 @@ static __device__ __noinline__ bool weight_kept_fp64(double v, double maxv, doub
 }
 
 template <class W> struct Stats {
-  W b1v, qmax;
-  int32_t b1i, valid, bad, qvalid, qbad;
+  W vmax, qmax;  // largest valid target value; largest proposal value (full q)
+  int32_t valid, bad, qvalid, qbad;
 };
 // Candidate tiles (32 tokens) a rank scans for list candidates before it
 // falls back to a full pass.
@@ -211,6 +211,7 @@ template <int DT> struct Row {
   cg::cluster_group cluster;
   int rank, ranks, row, lo, hi, groups;
   int xc;  // exchanges so far (the same on every rank)
+  int argmax_;  // the greedy token once argmax_id() has found it, else -1
 
   // Row-level values, identical on every rank after the statistics merge.
   Stats<W> all;
@@ -229,6 +230,7 @@ template <int DT> struct Row {
     hi = min(p.vocab, lo + p.slice_words * 32);
     groups = (hi - lo + 3) / 4;
     xc = 0;
+    argmax_ = -1;
     has_mask = p.mask != nullptr;
     resident = !p.stream_rows;
     vec = p.vector_load != 0;
@@ -332,10 +334,8 @@ template <int DT> struct Row {
 
   // ---- the statistics pass ----
   __device__ static Stats<W> merge_stats(Stats<W> a, Stats<W> b) {
-    const bool b_first = b.b1v > a.b1v || (b.b1v == a.b1v && b.b1i < a.b1i);
     Stats<W> m;
-    m.b1v = b_first ? b.b1v : a.b1v;
-    m.b1i = b_first ? b.b1i : a.b1i;
+    m.vmax = a.vmax > b.vmax ? a.vmax : b.vmax;
     m.qmax = a.qmax > b.qmax ? a.qmax : b.qmax;
     m.valid = a.valid + b.valid;
     m.bad = a.bad | b.bad;
@@ -347,7 +347,7 @@ template <int DT> struct Row {
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
       Stats<W> y;
-      y.b1v = shfl_xor(v.b1v, o); y.qmax = shfl_xor(v.qmax, o); y.b1i = shfl_xor(v.b1i, o);
+      y.vmax = shfl_xor(v.vmax, o); y.qmax = shfl_xor(v.qmax, o);
       y.valid = shfl_xor(v.valid, o); y.bad = shfl_xor(v.bad, o); y.qvalid = shfl_xor(v.qvalid, o);
       y.qbad = shfl_xor(v.qbad, o);
       v = merge_stats(v, y);
@@ -362,13 +362,17 @@ template <int DT> struct Row {
   // Statistics accumulated over groups.
   struct Acc {
     W best;
-    int best_i, valid, bad;
+    int valid, bad;
   };
   // Groups [g_begin, g_end) of the slice (g_begin a multiple of 8; every
   // tile either wholly inside or the slice's last): NaN / +inf anywhere
-  // (even masked), valid count, the maximum with the lowest ID among equals,
-  // and each 32-token tile's maximum. Warp-uniform: the 8 lanes of a tile
-  // combine its maximum by shuffles.
+  // (even masked), the valid count, the maximum, and each 32-token tile's
+  // maximum. The 8 lanes of a tile combine its maximum by shuffles.
+  //
+  // A whole unmasked group takes the short path: the sum of its four values
+  // scaled by 1/4 is NaN or +inf exactly when one of them is (four finite
+  // quarters cannot overflow, and -inf + +inf is NaN), and -inf exactly when
+  // one is -inf otherwise; -inf values are counted only then.
   template <class Load> __device__ __forceinline__ void stats_groups(int g_begin, int g_end, Load load, Acc& a) {
     for (int base = g_begin + warp_id() * 32; base < g_end; base += THREADS) {
       const int g = base + lane_id();
@@ -376,20 +380,28 @@ template <int DT> struct Row {
       if (g < g_end) {
         W v[4];
         load(g, v);
-        const unsigned bits = group_bits(g);
-        const int inside = min(4, hi - lo - 4 * g);
+        if (!has_mask && 4 * g + 4 <= hi - lo) {
+          const W q = (v[0] * W(0.25) + v[1] * W(0.25)) + (v[2] * W(0.25) + v[3] * W(0.25));
+          a.bad |= !(q < W(INFINITY));
+          int n = 4;
+          if (q == W(-INFINITY))
+            n = int(v[0] > W(-INFINITY)) + int(v[1] > W(-INFINITY)) + int(v[2] > W(-INFINITY)) +
+                int(v[3] > W(-INFINITY));
+          a.valid += n;
+          const W m01 = v[0] > v[1] ? v[0] : v[1], m23 = v[2] > v[3] ? v[2] : v[3];
+          tile = m01 > m23 ? m01 : m23;
+        } else {
+          const unsigned bits = group_bits(g);
+          const int inside = hi - lo - 4 * g;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if (j < inside) a.bad |= !(v[j] < W(INFINITY)) & (v[j] != W(-INFINITY));  // NaN or +inf
-          const bool ok = ((bits >> j) & 1u) && v[j] > W(-INFINITY);
-          const W x = ok ? v[j] : W(-INFINITY);
-          a.valid += ok;
-          if (x > a.best) {  // IDs rise within a thread, so ties keep the lowest
-            a.best = x;
-            a.best_i = lo + 4 * g + j;
+          for (int j = 0; j < 4; ++j) {
+            if (j < inside) a.bad |= !(v[j] < W(INFINITY)) & (v[j] != W(-INFINITY));  // NaN or +inf
+            const bool ok = ((bits >> j) & 1u) && v[j] > W(-INFINITY);
+            a.valid += ok;
+            if (ok && v[j] > tile) tile = v[j];
           }
-          tile = x > tile ? x : tile;
         }
+        if (tile > a.best) a.best = tile;
       }
 #pragma unroll
       for (int o = 1; o < 8; o <<= 1) {
@@ -398,6 +410,47 @@ template <int DT> struct Row {
       }
       if ((lane_id() & 7) == 0 && g < g_end) tmax[g >> 3] = tile;
     }
+  }
+  // Tiles (32 tokens) of this rank's slice; the last may be partial.
+  __device__ __forceinline__ int tile_count() const { return (groups + 7) / 8; }
+  // Local token i of the slice (0 <= i < hi - lo): its value and whether the
+  // mask allows it.
+  __device__ __forceinline__ W value_local(int i) const {
+    return resident ? widen(slice[i]) : widen(grow[int64_t(i) * gs]);
+  }
+  __device__ __forceinline__ bool allowed_local(int i) const {
+    if (!has_mask) return true;
+    const uint32_t word = resident ? mask_s[i >> 5]
+                                   : uint32_t(p.mask[int64_t(row) * p.m_s0 + int64_t((lo >> 5) + (i >> 5)) * p.m_s1]);
+    return (word >> (i & 31)) & 1u;
+  }
+  // The lowest-ID valid token of this rank's slice whose value is `target`
+  // (INT_MAX if none). Only the first tile whose maximum reaches `target`
+  // is read, so `target` must be at least every valid value of the slice
+  // that precedes it (the row or slice maximum). Block-uniform.
+  __device__ int first_at_value(W target) {
+    int first_tile = INT_MAX;
+    for (int t = threadIdx.x; t < tile_count(); t += THREADS)
+      if (tmax[t] >= target) {
+        first_tile = t;  // a thread's tiles ascend: its first hit is its lowest
+        break;
+      }
+    first_tile = block_all(first_tile, [](int x, int y) { return x < y ? x : y; }, s.red.ints);
+    int found = INT_MAX;
+    if (first_tile != INT_MAX && warp_id() == 0) {
+      const int i = 32 * first_tile + lane_id();
+      const bool hit = i < hi - lo && allowed_local(i) && value_local(i) == target;
+      const unsigned b = __ballot_sync(0xffffffffu, hit);
+      if (b) found = lo + 32 * first_tile + __ffs(b) - 1;
+    }
+    return block_all(found, [](int x, int y) { return x < y ? x : y; }, s.red.ints);
+  }
+  // The row's greedy token: the lowest ID whose value is the row maximum,
+  // over the cluster (found on first use, then kept). Every thread of every
+  // rank calls it at the same point.
+  __device__ int argmax_id() {
+    if (argmax_ < 0) argmax_ = cluster_min(first_at_value(maxv));
+    return argmax_;
   }
   // Bytes of the slice the TMA ring carries (whole 16-byte units), in chunks.
   __device__ __forceinline__ uint32_t ring_bytes() const { return (uint32_t(hi - lo) * uint32_t(sizeof(T))) & ~15u; }
@@ -414,7 +467,7 @@ template <int DT> struct Row {
   // through the TMA ring (streamed, 16-byte aligned rows), or from global
   // memory; then the cluster merge. Returns false if a copy never arrived.
   __device__ bool stats_pass(bool full_q, bool timed_out) {
-    Acc a{W(-INFINITY), INT_MAX, 0, 0};
+    Acc a{W(-INFINITY), 0, 0};
     bool lost = timed_out;
     if (resident) {
       stats_groups(0, groups, [&](int g, W v[4]) { load4(slice + 4 * g, v); }, a);
@@ -450,7 +503,7 @@ template <int DT> struct Row {
       }
     lost = __syncthreads_or(lost);
     if (lost) a.bad = 1;  // a slice copy never arrived: the row is not trusted
-    const Stats<W> merged = block_stats(Stats<W>{a.best, qmax, a.best_i, a.valid, a.bad, qvalid, qbad});
+    const Stats<W> merged = block_stats(Stats<W>{a.best, qmax, a.valid, a.bad, qvalid, qbad});
     if (threadIdx.x == 0) s.stats[parity()] = merged;
     ES_TRACE(p.workspace, p.rows, row, rank, 8);
     exchange();
@@ -459,7 +512,7 @@ template <int DT> struct Row {
     __syncthreads();
     all = s.peers.stats[0];
     for (int r = 1; r < ranks; ++r) all = merge_stats(all, s.peers.stats[r]);
-    maxv = all.b1v;
+    maxv = all.vmax;
     __syncthreads();
     return !lost;
   }
@@ -659,23 +712,29 @@ template <int DT> struct Row {
   }
   // The top-n valid tokens (and every token tied with the n-th) gathered to
   // rank 0. The ranks histogram their 32-token tiles by the distance of each
-  // tile's maximum below the row's; the first bin b where the cumulative tile
-  // count reaches n bounds the n-th token (every such tile has a token within
-  // bin b), so every valid token with bin <= b is gathered, from those tiles
-  // only. Slots in rank 0's buffer come from an atomic counter there; each
-  // rank pushes its count to every rank before the closing exchange. Returns
-  // the count, or -1 if no bin below 64 logits qualifies or the tokens do not
-  // fit the buffer (the caller then radix-selects).
+  // tile's maximum below the row's (shared-memory atomics); the first bin b
+  // where the cumulative tile count reaches n bounds the n-th token (every
+  // such tile has a token within bin b), so every valid token with bin <= b
+  // is gathered, from those tiles only: they are listed, then read by one
+  // warp each (one token per lane). Slots in rank 0's buffer come from an
+  // atomic counter there, one per warp and tile; each rank pushes its count
+  // to every rank before the closing exchange. Returns the count, or -1 if
+  // no bin below 64 logits qualifies or the tokens do not fit the buffer
+  // (the caller then radix-selects).
   __device__ int gather_near(int n) {
     uint32_t* h = s.hist[parity()];
     for (int i = threadIdx.x; i < RADIX; i += THREADS) h[i] = 0;
-    if (threadIdx.x == 0) s.n_cand = 0;
+    if (threadIdx.x == 0) {
+      s.n_cand = 0;
+      s.n_tiles = 0;
+    }
     __syncthreads();
-    const int n_tiles = (groups + 7) / 8;
-    for (int base = warp_id() * 32; base < n_tiles; base += THREADS) {
-      const int t = base + lane_id();
-      const int b = t < n_tiles && tmax[t] > W(-INFINITY) ? min(dist_bin(tmax[t]), DIST_BINS) : -1;
-      warp_bucket_add(nullptr, h, b, 0);
+    const int nt = tile_count();
+    for (int t = threadIdx.x; t < nt; t += THREADS) {
+      const W m = tmax[t];
+      if (!(m > W(-INFINITY))) continue;  // no valid token in the tile
+      const int b = dist_bin(m);
+      if (b < DIST_BINS) atomicAdd(&h[b], 1u);
     }
     exchange();
     int cnt = 0;
@@ -685,31 +744,57 @@ template <int DT> struct Row {
     const int cum = block_scan(cnt, s.red.ints, &total);
     if (threadIdx.x == 0) s.ival[0] = -1;
     __syncthreads();
-    if (cum >= n && cum - cnt < n) s.ival[0] = threadIdx.x;
+    if (int(threadIdx.x) < DIST_BINS && cum >= n && cum - cnt < n) s.ival[0] = threadIdx.x;
     __syncthreads();
     const int window = s.ival[0];
     ES_TRACE(p.workspace, p.rows, row, rank, 4);
-    if (window < 0) return -1;
+    if (window < 0) return -1;  // the same on every rank
+    // List this rank's tiles within the window.
+    for (int t = threadIdx.x; t < nt; t += THREADS) {
+      const W m = tmax[t];
+      if (m > W(-INFINITY) && dist_bin(m) <= window) {
+        const int at_ = atomicAdd(&s.n_tiles, 1);
+        if (at_ < TILE_CAP) s.tiles[at_] = t;
+      }
+    }
+    __syncthreads();
+    const int listed = s.n_tiles;
     int* counter = peer(&s.n_cand, 0);
     uint64_t* keys = peer(s.u.cand.key, 0);
     int32_t* ids = peer(s.u.cand.id, 0);
-    int mine = 0;
-    for (int g = threadIdx.x; g < groups; g += THREADS) {
-      if (dist_bin(tmax[g >> 3]) > window) continue;  // the tile's maximum is farther: so are its tokens
-      W v[4];
-      const unsigned bits = group(g, v);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (!((bits >> j) & 1u) || dist_bin(v[j]) > window) continue;
-        ++mine;
-        const int at_ = atomicAdd(counter, 1);
+    int mine = 0;  // tokens this warp gathered (the same in every lane)
+    // One tile, read by the whole warp (warp-uniform call).
+    auto take_tile = [&](int t) {
+      const int i = 32 * t + lane_id();
+      bool hit = false;
+      W v = W(-INFINITY);
+      if (i < hi - lo) {
+        v = value_local(i);
+        hit = allowed_local(i) && v > W(-INFINITY) && dist_bin(v) <= window;
+      }
+      const unsigned b = __ballot_sync(0xffffffffu, hit);
+      if (b == 0) return;
+      int base = 0;
+      if (lane_id() == 0) base = atomicAdd(counter, __popc(b));
+      base = __shfl_sync(0xffffffffu, base, 0);
+      if (hit) {
+        const int at_ = base + __popc(b & ((1u << lane_id()) - 1u));
         if (at_ < CAP) {
-          keys[at_] = uint64_t(order_key(v[j]));
-          ids[at_] = lo + 4 * g + j;
+          keys[at_] = uint64_t(order_key(v));
+          ids[at_] = lo + i;
         }
       }
+      mine += __popc(b);
+    };
+    if (listed <= TILE_CAP) {
+      for (int k = warp_id(); k < listed; k += WARPS) take_tile(s.tiles[k]);
+    } else {  // too many tiles to list: every warp walks the tile maxima
+      for (int t = warp_id(); t < nt; t += WARPS) {
+        const W m = tmax[t];
+        if (m > W(-INFINITY) && dist_bin(m) <= window) take_tile(t);
+      }
     }
-    mine = block_all(mine, [](int a, int b) { return a + b; }, s.red.ints);
+    mine = block_all(lane_id() == 0 ? mine : 0, [](int x, int y) { return x + y; }, s.red.ints);
     if (int(threadIdx.x) < ranks) peer(s.pushed, threadIdx.x)[rank] = mine;
     exchange();
     int gathered = 0;
@@ -852,7 +937,7 @@ template <int DT> struct Row {
         if (target <= 1.0) {
           // The first kept token (the maximum, weight exactly 1) reaches it.
           *normalizer = 1.0;
-          return Cut<Key>{1, order_key(maxv), all.b1i};
+          return Cut<Key>{1, order_key(maxv), argmax_id()};
         }
       }
       bool near = false;
@@ -913,11 +998,12 @@ template <int DT> struct Row {
   // whose bound reaches the FP32 winner's lower bound when the certificate
   // fails (or of every token, with exact_only). Returns -1 if none is kept.
   template <class Kept> __device__ int draw(uint32_t sub, int excluded, Kept kept, bool exact_only) {
+    // A kept token's score bounds the winner's from below: the maximum
+    // (x = 0), unless it is excluded.
+    const int greedy = argmax_id();
     if (threadIdx.x == 0) {
-      // A kept token's score bounds the winner's from below: the maximum
-      // (x = 0), or the runner-up when the maximum is excluded.
       float floor = -INFINITY;
-      const int t = all.b1i != excluded ? all.b1i : INT_MAX;
+      const int t = greedy != excluded ? greedy : INT_MAX;
       if (t != INT_MAX && valid_global(t)) {
         const W v = value_global(t);
         const float x = x32(v);
