@@ -68,6 +68,88 @@ template <int DT> struct RowKernel {
     return y > W(-INFINITY) ? exp(double(y) - double(r.all.qmax)) / sq : 0.0;
   }
 
+  // Warp 0 of rank 0 finishes a sorted list of n_keep <= 32 kept tokens,
+  // one per lane: the steps and FP64 formulas of list_finish below, with
+  // warp shuffles and ballots in place of block reductions and barriers.
+  __device__ static void finish_small(R& r, const RowCtx& c, int n_keep, bool verify, bool full_q, double sq,
+                                      double u_accept, RowResult& res) {
+    constexpr unsigned ALL = 0xffffffffu;
+    const int i = lane_id();
+    const bool in = i < n_keep;
+    const int id = in ? r.s.u.cand.id[i] : INT_MAX;
+    double w = 0;
+    bool ok = false;
+    if (in) {
+      w = exp(r.x64(key_value(Key(r.s.u.cand.key[i]))));
+      ok = w >= r.min_p && w > 0;
+    }
+    // min-p and positivity remove a suffix of the order.
+    const unsigned out = __ballot_sync(ALL, in && !ok);
+    const int n1 = out ? min(n_keep, __ffs(out) - 1) : n_keep;
+    // Inclusive prefix sums of the exact weights; lanes from n1 on add zero.
+    u128 prefix = i < n1 ? fx_of(w) : u128(0);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint64_t lo = __shfl_up_sync(ALL, uint64_t(prefix), o);
+      const uint64_t hi = __shfl_up_sync(ALL, uint64_t(prefix >> 64), o);
+      if (i >= o) prefix += (u128(hi) << 64) | lo;
+    }
+    auto prefix_at = [&](int lane) {
+      const uint64_t lo = __shfl_sync(ALL, uint64_t(prefix), lane);
+      const uint64_t hi = __shfl_sync(ALL, uint64_t(prefix >> 64), lane);
+      return (u128(hi) << 64) | lo;
+    };
+    bool near = false;
+    const double d1 = fx_round(prefix_at(31), uint32_t(n1), &near);
+    r.count_near_tie(near);
+    int n2 = n1;
+    double denominator = d1;
+    if (r.top_p < 1) {
+      const double target = r.top_p * d1;
+      if (target <= 1.0) {
+        n2 = 1;  // the first token's weight is exactly 1
+      } else {
+        bool nr = false;
+        const bool reach = i < n1 && fx_reaches(prefix, uint32_t(i + 1), target, &nr);
+        const unsigned hits = __ballot_sync(ALL, reach);
+        n2 = hits ? __ffs(hits) : n1;
+      }
+      denominator = fx_round(prefix_at(n2 - 1), uint32_t(n2), &near);
+      r.count_near_tie(near);
+    }
+    const double prob = i < n2 ? w / denominator : 0.0;
+    // One draw over the list: argmax log(p) + G, lowest ID on ties.
+    auto draw_list = [&](uint32_t sub, int excluded) {
+      Best b = no_best();
+      if (i < n2 && id != excluded && prob > 0) b = Best{log(prob) + noise64(r.addr.word(sub, uint32_t(id))), id};
+      b = warp_all(b, [](Best a, Best c2) { return best_of(a, c2); });
+      return b.id == INT_MAX ? -1 : b.id;
+    };
+    if (!verify) {
+      res.sample = draw_list(0, -1);
+      return;
+    }
+    const unsigned at_draft = __ballot_sync(ALL, i < n2 && id == c.draft_id);
+    const double p_draft = __shfl_sync(ALL, prob, at_draft ? __ffs(at_draft) - 1 : 0);
+    const double px = at_draft ? p_draft : 0.0;
+    const double qx = q_of_draft(r, c, full_q, sq);
+    res.accept = u_accept < fmin(1.0, px / qx);
+    if (res.accept) return;
+    if (!full_q) {
+      res.residual = draw_list(2, c.draft_id);
+      return;
+    }
+    Best b = no_best();
+    if (i < n2 && prob > 0) {
+      const W y = r.q_value(id);
+      const double q = y > W(-INFINITY) ? exp(double(y) - double(r.all.qmax)) / sq : 0.0;
+      const double rr = fmax(prob - q, 0.0);
+      if (rr > 0) b = Best{log(rr) + noise64(r.addr.word(2, uint32_t(id))), id};
+    }
+    b = warp_all(b, [](Best a, Best c2) { return best_of(a, c2); });
+    res.residual = b.id == INT_MAX ? -1 : b.id;
+  }
+
   // Rank 0 finishes a list row: the m gathered candidates hold the kept
   // n_keep tokens first once sorted. Oracle formulas throughout (FP64).
   __device__ static void list_finish(R& r, const RowCtx& c, int m, int n_keep, bool verify, bool full_q, double sq,
@@ -75,6 +157,10 @@ template <int DT> struct RowKernel {
     auto& s = r.s;
     r.sort_candidates(m);
     ES_TRACE(r.p.workspace, r.p.rows, r.row, r.rank, 10);
+    if (n_keep <= 32) {
+      if (warp_id() == 0) finish_small(r, c, n_keep, verify, full_q, sq, u_accept, res);
+      return;
+    }
     const int i = threadIdx.x;
     const bool in = i < n_keep;
     const int id = in ? s.u.cand.id[i] : INT_MAX;

@@ -6,6 +6,7 @@
 namespace es {
 
 constexpr int LIST_MAX = 256;   // largest kept set finished as an FP64 list (the plan's list_max caps it)
+static_assert(THREADS >= LIST_MAX, "one thread per list entry");
 constexpr int CAP = 1024;       // candidate buffer of a list row (cluster rank 0's shared memory)
 constexpr int DIST_BINS = 128;  // distance-below-maximum bins of 0.5 logit, plus one "far" bin
 constexpr int RADIX = 256;      // digits per radix-select level

@@ -802,8 +802,56 @@ template <int DT> struct Row {
     return gathered <= CAP ? gathered : -1;
   }
 
-  // Sorts rank 0's m candidates into (key desc, ID asc) order (bitonic).
+  // Sorts rank 0's m candidates into (key desc, ID asc) order (bitonic):
+  // up to 32 within warp 0's registers, more in shared memory.
   __device__ void sort_candidates(int m) {
+    if (m <= 32) {
+      if (warp_id() == 0) {
+        const int i = lane_id();
+        uint64_t key = i < m ? s.u.cand.key[i] : 0;  // empty lanes sort last
+        int32_t id = i < m ? s.u.cand.id[i] : INT_MAX;
+#pragma unroll
+        for (int k = 2; k <= 32; k <<= 1)
+#pragma unroll
+          for (int j = k >> 1; j > 0; j >>= 1) {
+            const uint64_t other_key = __shfl_xor_sync(0xffffffffu, key, j);
+            const int32_t other_id = __shfl_xor_sync(0xffffffffu, id, j);
+            const bool mine_first = key > other_key || (key == other_key && id < other_id);
+            const bool keep_first = ((i & j) == 0) == ((i & k) == 0);
+            if (mine_first != keep_first) {
+              key = other_key;
+              id = other_id;
+            }
+          }
+        s.u.cand.key[i] = key;
+        s.u.cand.id[i] = id;
+      }
+      __syncthreads();
+      return;
+    }
+    if (m <= LIST_MAX) {
+      // Rank sort: each candidate's position is the number of candidates
+      // before it in the order ((key, ID) pairs are distinct), then one scatter.
+      const int i = threadIdx.x;
+      uint64_t key = 0;
+      int32_t id = INT_MAX;
+      int rank_i = 0;
+      if (i < m) {
+        key = s.u.cand.key[i];
+        id = s.u.cand.id[i];
+        for (int j = 0; j < m; ++j) {
+          const uint64_t kj = s.u.cand.key[j];
+          rank_i += kj > key || (kj == key && s.u.cand.id[j] < id);
+        }
+      }
+      __syncthreads();
+      if (i < m) {
+        s.u.cand.key[rank_i] = key;
+        s.u.cand.id[rank_i] = id;
+      }
+      __syncthreads();
+      return;
+    }
     int size = 1;
     while (size < m) size <<= 1;
     uint64_t* key = s.u.cand.key;
