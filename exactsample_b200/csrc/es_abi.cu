@@ -157,13 +157,13 @@ constexpr size_t RESIDENT_BYTES = 80 * 1024;
 constexpr int SM_COUNT = 148, RESIDENT_SLOTS = 2 * SM_COUNT;
 constexpr size_t MAX_SMEM = 227 * 1024;
 
-template <int DT> size_t smem_for(int sw, bool stream) { return es::smem_bytes<DT>(sw, stream); }
-size_t smem_for_dtype(int dtype, int sw, bool stream) {
+template <int DT> size_t smem_for(int sw, int stages) { return es::smem_bytes<DT>(sw, stages); }
+size_t smem_for_dtype(int dtype, int sw, int stages) {
   switch (dtype) {
-    case ES_F32: return smem_for<ES_F32>(sw, stream);
-    case ES_F64: return smem_for<ES_F64>(sw, stream);
-    case ES_F16: return smem_for<ES_F16>(sw, stream);
-    default: return smem_for<ES_BF16>(sw, stream);
+    case ES_F32: return smem_for<ES_F32>(sw, stages);
+    case ES_F64: return smem_for<ES_F64>(sw, stages);
+    case ES_F16: return smem_for<ES_F16>(sw, stages);
+    default: return smem_for<ES_BF16>(sw, stages);
   }
 }
 
@@ -192,15 +192,26 @@ int choose_cluster(int64_t rows, int64_t vocab, int dtype, int* slice_words, siz
     if (forced[0] == '0') streamed = false;
     if (forced[0] == '1') streamed = true;
   }
+  // The TMA ring: four 16 KB stages while every rank has a place on the GPU
+  // with two per SM; two stages beyond that, so that three ranks fit an SM
+  // (EXACTSAMPLE_RING=2..4 forces the depth).
+  int stages = 0;
+  if (streamed) {
+    stages = rows * c > RESIDENT_SLOTS ? 2 : es::MAX_RING_STAGES;
+    if (const char* forced = std::getenv("EXACTSAMPLE_RING")) {
+      const int n = std::atoi(forced);
+      if (n >= 2 && n <= es::MAX_RING_STAGES) stages = n;
+    }
+  }
   for (;; ++c) {
     if (c > 16) return -1;
     const int sw = int((words + c - 1) / c);
     const int used = int((words + sw - 1) / sw);  // no empty ranks
-    const size_t bytes = smem_for_dtype(dtype, sw, streamed);
+    const size_t bytes = smem_for_dtype(dtype, sw, stages);
     if (bytes <= MAX_SMEM) {
       *slice_words = sw;
       *smem = bytes;
-      *stream = streamed;
+      *stream = stages;
       return used;
     }
   }

@@ -20,9 +20,10 @@ template <int DT> __host__ __device__ constexpr size_t smem_tmax(int slice_words
 template <int DT> __host__ __device__ constexpr size_t smem_slice(int slice_words, bool stream) {
   return smem_tmax<DT>(slice_words, stream) + align_up(size_t(slice_words) * sizeof(typename Types<DT>::W), 128);
 }
-template <int DT> __host__ __device__ constexpr size_t smem_bytes(int slice_words, bool stream) {
+template <int DT> __host__ __device__ constexpr size_t smem_bytes(int slice_words, int ring_stages) {
+  const bool stream = ring_stages > 0;
   return smem_slice<DT>(slice_words, stream) +
-         (stream ? size_t(RING_STAGES) * RING_CHUNK
+         (stream ? size_t(ring_stages) * RING_CHUNK
                  : align_up(size_t(slice_words) * 32 * sizeof(typename Types<DT>::T), 128));
 }
 
@@ -289,7 +290,10 @@ template <int DT> struct RowKernel {
   }
 };
 
-template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const __grid_constant__ Params p) {
+// MIN_BLOCKS: resident CTAs per SM the register allocation must allow (3 for
+// large streamed batches with the 2-stage ring, else 2).
+template <int DT, int MIN_BLOCKS>
+__global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_constant__ Params p) {
   using K = RowKernel<DT>;
   using R = typename K::R;
   using T = typename K::T;
@@ -308,7 +312,7 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
   //    Resident rows copy the whole slice; streamed rows fill the TMA ring.
   if (threadIdx.x == 0) {
     mbar_init(&s.bar, 1);
-    for (int i = 0; i < RING_STAGES; ++i) mbar_init(&s.ring_bar[i], 1);
+    for (int i = 0; i < MAX_RING_STAGES; ++i) mbar_init(&s.ring_bar[i], 1);
     mbar_init_fence();
   }
   __syncthreads();
@@ -318,7 +322,7 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
     if (threadIdx.x == 0) {
       mbar_arrive_expect_tx(&s.bar, 0);
       if (p.vector_load)
-        for (int c = 0; c < min(RING_STAGES, r.ring_chunks()); ++c) r.ring_issue(c);
+        for (int c = 0; c < min(p.stream_rows, r.ring_chunks()); ++c) r.ring_issue(c);
     }
   } else if (p.vector_load) {
     const uint32_t bytes = uint32_t(n) * uint32_t(sizeof(T)), bulk = bytes & ~15u;
@@ -362,7 +366,7 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
   __syncthreads();
   if (s.ctx.skip) {  // the same decision on every rank; no rank reads another's memory
     if (stream && p.vector_load && threadIdx.x == 0)  // let the ring copies land before leaving
-      for (int c = 0; c < min(RING_STAGES, r.ring_chunks()); ++c)
+      for (int c = 0; c < min(p.stream_rows, r.ring_chunks()); ++c)
         for (uint32_t spins = 0; !mbar_try_wait(&s.ring_bar[c], 0) && spins < (1u << 22); ++spins) {
         }
     return;
@@ -426,8 +430,8 @@ template <int DT> __global__ void __launch_bounds__(THREADS) rows_kernel(const _
 // Launch of the row kernel: a (C, rows) grid of C-block clusters, with
 // programmatic stream serialization after the preparation kernel.
 template <int DT> cudaError_t launch_rows(const Params& p, int cluster, cudaStream_t stream) {
-  const size_t smem = smem_bytes<DT>(p.slice_words, p.stream_rows != 0);
-  auto kernel = rows_kernel<DT>;
+  const size_t smem = smem_bytes<DT>(p.slice_words, p.stream_rows);
+  auto kernel = p.stream_rows == 2 ? rows_kernel<DT, 3> : rows_kernel<DT, 2>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   if (cluster > 8) {

@@ -10,7 +10,7 @@ static_assert(THREADS >= LIST_MAX, "one thread per list entry");
 constexpr int CAP = 1024;       // candidate buffer of a list row (cluster rank 0's shared memory)
 constexpr int DIST_BINS = 128;  // distance-below-maximum bins of 0.5 logit, plus one "far" bin
 constexpr int RADIX = 256;      // digits per radix-select level
-constexpr int RING_STAGES = 4;         // streamed rows: TMA ring depth
+constexpr int MAX_RING_STAGES = 4;     // streamed rows: deepest TMA ring
 constexpr uint32_t RING_CHUNK = 16384; // bytes per ring stage (a multiple of 32 tokens of any dtype)
 
 // Kernel arguments (filled by es_verify from es_args); strides in elements.
@@ -56,7 +56,7 @@ struct Params {
   int32_t vector_load;     // rows contiguous and 16-byte aligned: TMA bulk loads
   int32_t offsets_inline;  // the preparation kernel validates cu_rows itself
   int32_t exact_draws;     // dispatch="reference": every draw scored in FP64, no lists
-  int32_t stream_rows;     // rows stream through a TMA ring instead of staying in shared memory
+  int32_t stream_rows;     // 0: rows stay in shared memory; else the depth (2..4) of the TMA ring they stream through
 };
 
 // Per-row outcome, written by the row's cluster rank 0 and read by whichever

@@ -117,7 +117,7 @@ constexpr int TILE_CAP = 256;
 
 template <class W> struct Smem {
   uint64_t bar;
-  uint64_t ring_bar[RING_STAGES];
+  uint64_t ring_bar[MAX_RING_STAGES];
   int32_t timeout;
   RowCtx ctx;
   // Published to the other ranks, double-buffered by exchange parity.
@@ -458,9 +458,10 @@ template <int DT> struct Row {
   // Thread 0 starts the TMA copy of chunk c into its ring stage.
   __device__ __forceinline__ void ring_issue(int c) {
     const uint32_t off = uint32_t(c) * RING_CHUNK, len = min(RING_CHUNK, ring_bytes() - off);
-    uint64_t* bar = &s.ring_bar[c % RING_STAGES];
+    const int stage = c % p.stream_rows;
+    uint64_t* bar = &s.ring_bar[stage];
     mbar_arrive_expect_tx(bar, len);
-    bulk_load(reinterpret_cast<uint8_t*>(slice) + (c % RING_STAGES) * RING_CHUNK,
+    bulk_load(reinterpret_cast<uint8_t*>(slice) + stage * RING_CHUNK,
               reinterpret_cast<const uint8_t*>(grow) + off, len, bar);
   }
   // The statistics pass over the whole slice: from shared memory (resident),
@@ -474,19 +475,19 @@ template <int DT> struct Row {
     } else if (vec) {
       constexpr int GPC = int(RING_CHUNK / (4 * sizeof(T)));  // groups per chunk
       const int ring_groups = int(ring_bytes() / (4 * sizeof(T))) & ~7;  // whole tiles
-      const int chunks = ring_chunks();
+      const int chunks = ring_chunks(), stages = p.stream_rows;
       for (int c = 0; c < chunks; ++c) {
         uint32_t spins = 0;
-        while (!mbar_try_wait(&s.ring_bar[c % RING_STAGES], uint32_t(c / RING_STAGES) & 1u))
+        while (!mbar_try_wait(&s.ring_bar[c % stages], uint32_t(c / stages) & 1u))
           if (++spins >= (1u << 22)) {
             lost = true;
             break;
           }
-        const T* stage = slice + (c % RING_STAGES) * (RING_CHUNK / sizeof(T)) - int64_t(c) * GPC * 4;
+        const T* stage = slice + (c % stages) * (RING_CHUNK / sizeof(T)) - int64_t(c) * GPC * 4;
         stats_groups(c * GPC, min((c + 1) * GPC, ring_groups),
                      [&](int g, W v[4]) { load4(stage + 4 * g, v); }, a);
         __syncthreads();  // every thread is done with this stage
-        if (threadIdx.x == 0 && c + RING_STAGES < chunks) ring_issue(c + RING_STAGES);
+        if (threadIdx.x == 0 && c + stages < chunks) ring_issue(c + stages);
       }
       stats_groups(ring_groups, groups, [&](int g, W v[4]) { values(g, v); }, a);  // the last partial tile
     } else {

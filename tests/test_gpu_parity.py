@@ -294,3 +294,14 @@ def test_results_do_not_depend_on_the_row_mode(stream, monkeypatch):
         for list_max in [256, 0]:
             assert_same(run_abi(device_inputs(case), mode=case["mode"], list_max=list_max), expected,
                         context=case["name"])
+
+
+@pytest.mark.parametrize("ring", ["2", "3", "4"])
+def test_results_do_not_depend_on_the_ring_depth(ring, monkeypatch):
+    """Streamed rows give identical results with a 2-, 3- or 4-stage TMA ring."""
+    monkeypatch.setenv("EXACTSAMPLE_STREAM", "1")
+    monkeypatch.setenv("EXACTSAMPLE_RING", ring)
+    for entry in _large():
+        name, subset, digest, expected = entry
+        case = golden_io.large_case(name, subset, digest)
+        assert_same(run_abi(device_inputs(case), mode=case["mode"]), expected, context=f"{name} ring={ring}")
