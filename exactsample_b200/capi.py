@@ -15,8 +15,10 @@ ES_F32, ES_F64, ES_F16, ES_BF16, ES_I32, ES_I64, ES_U8 = range(7)
 ERRORS = {0: "ES_SUCCESS", -1: "ES_ERR_ARGUMENT", -2: "ES_ERR_CAPACITY", -3: "ES_ERR_ALIGNMENT",
           -4: "ES_ERR_ALIAS", -5: "ES_ERR_UNSUPPORTED", -6: "ES_ERR_LAUNCH", -7: "ES_ERR_DEVICE"}
 # Every function the header declares.
-EXPORTS = ["es_workspace_bytes", "es_verify", "es_verify_timed", "es_verify_static", "es_last_error",
-           "es_abi_version"]
+EXPORTS = ["es_workspace_bytes", "es_verify", "es_verify_timed", "es_verify_static", "es_verify_sharded",
+           "es_shard_signal", "es_shard_wait", "es_ipc_alloc", "es_ipc_open", "es_ipc_close", "es_ipc_free",
+           "es_last_error", "es_abi_version"]
+MAX_SHARDS = 8  # ES_MAX_SHARDS
 STATIC_MAX_ROWS = 4096  # ES_STATIC_MAX_ROWS
 
 
@@ -34,6 +36,15 @@ class Args(ctypes.Structure):
     _fields_ = [(name, Tensor) for name in FIELDS] + [
         ("mode", ctypes.c_int64), ("dispatch", ctypes.c_int64), ("max_draft", ctypes.c_int64),
         ("list_max", ctypes.c_int64)]
+
+
+class Shards(ctypes.Structure):
+    """es_shards: one GPU's view of a vocabulary-sharded call."""
+    _fields_ = [("count", ctypes.c_int32), ("rank", ctypes.c_int32), ("cols", ctypes.c_int64),
+                ("vocab", ctypes.c_int64), ("req_begin", ctypes.c_int64), ("req_end", ctypes.c_int64),
+                ("epoch", ctypes.c_uint64)] + [
+        (name, ctypes.c_void_p * MAX_SHARDS)
+        for name in ["target", "draft", "tokens", "accepted", "status", "path", "ready"]]
 
 
 _lib = None
@@ -56,6 +67,21 @@ def load(path: str | Path | None = None) -> ctypes.CDLL:
         lib.es_verify_timed.restype = ctypes.c_int
         lib.es_verify_static.argtypes = [ctypes.POINTER(Args), ctypes.c_void_p]
         lib.es_verify_static.restype = ctypes.c_int
+        lib.es_verify_sharded.argtypes = [ctypes.POINTER(Args), ctypes.POINTER(Shards), ctypes.c_void_p]
+        lib.es_verify_sharded.restype = ctypes.c_int
+        lib.es_shard_signal.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]
+        lib.es_shard_signal.restype = ctypes.c_int
+        lib.es_shard_wait.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, ctypes.c_uint64,
+                                      ctypes.c_void_p, ctypes.c_void_p]
+        lib.es_shard_wait.restype = ctypes.c_int
+        lib.es_ipc_alloc.argtypes = [ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p]
+        lib.es_ipc_alloc.restype = ctypes.c_int
+        lib.es_ipc_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]
+        lib.es_ipc_open.restype = ctypes.c_int
+        lib.es_ipc_close.argtypes = [ctypes.c_void_p]
+        lib.es_ipc_close.restype = ctypes.c_int
+        lib.es_ipc_free.argtypes = [ctypes.c_void_p]
+        lib.es_ipc_free.restype = ctypes.c_int
         lib.es_last_error.argtypes = []
         lib.es_last_error.restype = ctypes.c_char_p
         lib.es_abi_version.argtypes = []
@@ -124,3 +150,18 @@ def call(tensors: dict, *, mode: int = 0, dispatch: int = 0, max_draft: int = 0,
                                    ctypes.c_void_p(after.cuda_event if after is not None else 0))
     if code != 0:
         raise AbiError(code, lib.es_last_error().decode())
+
+
+def check(code: int) -> None:
+    """Raises AbiError for a non-zero return code of the C ABI."""
+    if code != 0:
+        raise AbiError(code, load().es_last_error().decode())
+
+
+def args_of(tensors: dict, *, mode: int = 0, dispatch: int = 0, max_draft: int = 0, list_max: int = 256) -> Args:
+    """An es_args for torch tensors keyed by field name (absent or None: an empty descriptor)."""
+    args = Args()
+    for name in FIELDS:
+        setattr(args, name, describe(tensors.get(name)))
+    args.mode, args.dispatch, args.max_draft, args.list_max = mode, dispatch, max_draft, list_max
+    return args

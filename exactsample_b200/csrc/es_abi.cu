@@ -41,11 +41,18 @@ __global__ void __launch_bounds__(128) prepare(const __grid_constant__ Params p)
   }
   const int64_t req = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (req >= p.requests) return;
-  for (int64_t i = 0; i <= p.max_draft; ++i) p.tokens[req * p.tok_s0 + i * p.tok_s1] = -1;
-  p.accepted[req * p.acc_s] = 0;
-  p.path[req * p.path_s] = p.exact_draws ? ES_PATH_REFERENCE : ES_PATH_FUSED;
+  // A vocabulary-sharded call resets only this GPU's requests, in every
+  // GPU's output buffers; their owners write the others.
+  const bool owned = p.sh.count <= 1 || (req >= p.sh.req_begin && req < p.sh.req_end);
   const int32_t status = bad ? ES_INVALID_INPUT : metadata_status(p, req);
-  p.status[req * p.st_s] = status;
+  if (owned)
+    for (int set = 0; set < output_sets(p); ++set) {
+      const Outputs o = output_set(p, set);
+      for (int64_t i = 0; i <= p.max_draft; ++i) o.tokens[req * p.tok_s0 + i * p.tok_s1] = -1;
+      o.accepted[req * p.acc_s] = 0;
+      o.path[req * p.path_s] = p.exact_draws ? ES_PATH_REFERENCE : ES_PATH_FUSED;
+      o.status[req * p.st_s] = status;
+    }
   if (bad) return;  // rows cannot be attributed; the row kernel reads the flag
   const int64_t begin = at(p.cu_rows, p.cu_s, req), end = at(p.cu_rows, p.cu_s, req + 1);
   if (begin < 0 || end > p.rows || begin >= end) return;
@@ -53,8 +60,8 @@ __global__ void __launch_bounds__(128) prepare(const __grid_constant__ Params p)
   c.req = int32_t(req);
   c.begin = int32_t(begin);
   c.end = int32_t(end);
-  c.skip = status != ES_OK;
-  if (status == ES_OK) {
+  c.skip = status != ES_OK || !owned;
+  if (!c.skip) {
     arrivals(p.workspace, p.rows)[begin] = 0;
     c.kind = int32_t(at(p.draft_kind, p.kind_s, req));
     c.top_k = int32_t(at(p.top_k, p.topk_s, req));
@@ -66,12 +73,36 @@ __global__ void __launch_bounds__(128) prepare(const __grid_constant__ Params p)
   }
   RowCtx* out = row_contexts(p.workspace, p.rows);
   for (int64_t row = begin; row < end; ++row) {
-    if (status == ES_OK) {
+    if (!c.skip) {
       c.position = uint32_t(at(p.positions, p.pos_s, row));
       c.draft_id = row + 1 < end ? int32_t(p.draft_ids[req * p.d_s0 + (row - begin) * p.d_s1]) : -1;
     }
     out[row] = c;
   }
+}
+
+// Vocabulary-sharded calls: a GPU's "shard written" and "outputs done" flags.
+// One thread stores `epoch` with system-scope release once the stream's
+// earlier work is done; one thread waits (bounded) until every listed flag
+// has reached `epoch`, counting a give-up in *timeouts.
+__global__ void signal_flag(uint64_t* flag, uint64_t epoch) {
+  __threadfence_system();
+  st_release_sys(flag, epoch);
+}
+struct FlagSet {
+  const uint64_t* flag[MAX_SHARDS];
+  int32_t count;
+  uint64_t epoch;
+  uint32_t* timeouts;
+};
+__global__ void wait_flags(const __grid_constant__ FlagSet f) {
+  for (int g = 0; g < f.count; ++g)
+    for (uint32_t spins = 0; ld_acquire_sys(f.flag[g]) < f.epoch;)
+      if (++spins >= (1u << 20)) {
+        if (f.timeouts != nullptr) atomicAdd(f.timeouts, 1u);
+        break;
+      }
+  __threadfence_system();
 }
 
 template <int DT> cudaError_t launch_rows(const Params& p, int cluster, cudaStream_t stream);
@@ -233,8 +264,10 @@ int device_check() {
 // reference's formula); otherwise the bytes of the library's static scratch
 // that a->workspace describes (es_verify_static), checked against what this
 // call's kernels actually use.
+// `sh`: a vocabulary-sharded call's shard table (NULL otherwise); its
+// target_logits (and draft_logits) are this GPU's shard.
 int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaEvent_t after,
-                uint64_t own_scratch = 0) {
+                uint64_t own_scratch = 0, const es_shards* sh = nullptr) {
   g_error.clear();
   if (a == nullptr) return fail(ES_ERR_ARGUMENT, "null arguments");
   const es_tensor& logits = a->target_logits;
@@ -245,7 +278,20 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
   if (logits.stride[0] < 0 || logits.stride[1] < 0) return fail(ES_ERR_ARGUMENT, "target_logits has a negative stride");
   if (!check(a->cu_rows, ES_I64, 1, "cu_rows")) return ES_ERR_ARGUMENT;
   if (a->cu_rows.size[0] < 1) return fail(ES_ERR_ARGUMENT, "cu_rows must contain an endpoint");
-  const int64_t requests = a->cu_rows.size[0] - 1, rows = logits.size[0], vocab = logits.size[1];
+  const int64_t requests = a->cu_rows.size[0] - 1, rows = logits.size[0];
+  int64_t vocab = logits.size[1];
+  if (sh != nullptr) {
+    if (!(sh->count >= 2 && sh->count <= es::MAX_SHARDS && sh->rank >= 0 && sh->rank < sh->count))
+      return fail(ES_ERR_ARGUMENT, "shards: count must be in [2, 8] and rank in [0, count)");
+    if (!(sh->cols > 0 && sh->cols % 16 == 0 && sh->vocab > (sh->count - 1) * sh->cols &&
+          sh->vocab <= sh->count * sh->cols && sh->vocab <= INT32_MAX))
+      return fail(ES_ERR_ARGUMENT, "shards: cols must be a positive multiple of 16 with (count - 1) * cols < vocab <= count * cols");
+    const int64_t width = std::min<int64_t>(sh->cols, sh->vocab - int64_t(sh->rank) * sh->cols);
+    if (logits.size[1] != width) return fail(ES_ERR_ARGUMENT, "shards: target_logits must be this GPU's shard [rows, its columns]");
+    if (!(sh->req_begin >= 0 && sh->req_begin <= sh->req_end && sh->req_end <= requests))
+      return fail(ES_ERR_ARGUMENT, "shards: the request range must lie in [0, requests]");
+    vocab = sh->vocab;
+  }
   if (requests == 0 && rows != 0) return fail(ES_ERR_ARGUMENT, "an empty request batch cannot contain target rows");
   if (!(vocab > 0 && vocab <= INT32_MAX && rows <= INT32_MAX && requests <= INT32_MAX))
     return fail(ES_ERR_ARGUMENT, "exactsample dimensions exceed int32 kernel indexing");
@@ -272,7 +318,7 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
   const bool has_draft = a->draft_logits.ndim != 0, has_mask = a->mask.ndim != 0;
   if (has_draft) {
     const es_tensor& q = a->draft_logits;
-    if (q.ndim != 2 || q.size[0] != rows || q.size[1] != vocab || q.stride[0] < 0 || q.stride[1] < 0 ||
+    if (q.ndim != 2 || q.size[0] != rows || q.size[1] != logits.size[1] || q.stride[0] < 0 || q.stride[1] < 0 ||
         (q.data == nullptr && numel(q) != 0))
       return fail(ES_ERR_ARGUMENT, "draft_logits shape/device mismatch");
     if (q.dtype != logits.dtype) return fail(ES_ERR_ARGUMENT, "draft_logits must have the target_logits dtype");
@@ -318,6 +364,26 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
     for (int j = 0; j < i; ++j)
       if (!disjoint(*outputs[i], *outputs[j])) return fail(ES_ERR_ALIAS, "exactsample outputs alias");
   }
+  if (sh != nullptr) {
+    // Every GPU's buffers, laid out as this GPU's.
+    for (int g = 0; g < sh->count; ++g)
+      if (sh->target[g] == nullptr || sh->ready[g] == nullptr || sh->tokens[g] == nullptr ||
+          sh->accepted[g] == nullptr || sh->status[g] == nullptr || sh->path[g] == nullptr ||
+          (has_draft && sh->draft[g] == nullptr))
+        return fail(ES_ERR_ARGUMENT, "shards: every GPU needs its shard, flag and output buffers");
+    if (sh->target[sh->rank] != logits.data || (has_draft && sh->draft[sh->rank] != a->draft_logits.data) ||
+        sh->tokens[sh->rank] != a->tokens.data || sh->accepted[sh->rank] != a->accepted_len.data ||
+        sh->status[sh->rank] != a->status.data || sh->path[sh->rank] != a->path_used.data)
+      return fail(ES_ERR_ARGUMENT, "shards: this GPU's entries must be the call's own tensors");
+    const size_t e = element_size(logits.dtype);
+    bool aligned = logits.stride[1] == 1 && (uint64_t(logits.stride[0]) * e) % 16 == 0;
+    for (int g = 0; g < sh->count; ++g) {
+      aligned &= reinterpret_cast<uintptr_t>(sh->target[g]) % 16 == 0;
+      if (has_draft) aligned &= reinterpret_cast<uintptr_t>(sh->draft[g]) % 16 == 0;
+    }
+    if (has_draft) aligned &= a->draft_logits.stride[1] == 1 && a->draft_logits.stride[0] == logits.stride[0];
+    if (!aligned) return fail(ES_ERR_ALIGNMENT, "shards: shard buffers must be contiguous rows on 16-byte boundaries");
+  }
   if (requests == 0) return ES_SUCCESS;
   const int dev = device_check();
   if (dev != ES_SUCCESS) return dev;
@@ -347,15 +413,35 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
   p.exact_draws = a->dispatch == ES_REFERENCE;
   p.list_max = p.exact_draws ? 0 : int32_t(a->list_max);
   p.offsets_inline = requests <= 8192;
+  if (sh != nullptr) {
+    es::Shards& t = p.sh;
+    t.count = sh->count;
+    t.rank = sh->rank;
+    t.cols = int32_t(sh->cols);
+    t.req_begin = int32_t(sh->req_begin);
+    t.req_end = int32_t(sh->req_end);
+    t.epoch = sh->epoch;
+    for (int g = 0; g < sh->count; ++g) {
+      t.target[g] = sh->target[g];
+      t.draft[g] = has_draft ? sh->draft[g] : nullptr;
+      t.tokens[g] = static_cast<int64_t*>(sh->tokens[g]);
+      t.accepted[g] = static_cast<int32_t*>(sh->accepted[g]);
+      t.status[g] = static_cast<int32_t*>(sh->status[g]);
+      t.path[g] = static_cast<int32_t*>(sh->path[g]);
+      t.ready[g] = sh->ready[g];
+    }
+  }
 
   int cluster = 1;
   size_t smem = 0;
   if (rows > 0) {
-    cluster = choose_cluster(rows, vocab, logits.dtype, &p.slice_words, &smem, &p.stream_rows);
+    // A sharded call finishes about rows / count of the rows on this GPU.
+    const int64_t busy = sh != nullptr ? (rows + sh->count - 1) / sh->count : rows;
+    cluster = choose_cluster(busy, vocab, logits.dtype, &p.slice_words, &smem, &p.stream_rows);
     if (cluster < 0) return fail(ES_ERR_UNSUPPORTED, "vocabulary too large for one 16-block cluster's shared memory");
     const size_t e = element_size(logits.dtype);
     p.vector_load = logits.stride[1] == 1 && reinterpret_cast<uintptr_t>(logits.data) % 16 == 0 &&
-                    (uint64_t(logits.stride[0]) * e) % 16 == 0;
+                    (uint64_t(logits.stride[0]) * e) % 16 == 0;  // always so for shards (checked above)
   }
   cudaGetLastError();  // clear a stale error so the checks below report this call's launches
   if (!p.offsets_inline) es::check_offsets<<<1, 1024, 0, stream>>>(p);
@@ -447,6 +533,83 @@ int es_verify_static(const es_args* args, void* stream) {
   a.workspace.dtype = ES_U8;
   a.workspace.ndim = 1;
   return verify_impl(&a, static_cast<cudaStream_t>(stream), nullptr, nullptr, STATIC_SCRATCH_BYTES);
+}
+
+int es_verify_sharded(const es_args* args, const es_shards* shards, void* stream) {
+  if (shards == nullptr) {
+    g_error = "null shards";
+    return ES_ERR_ARGUMENT;
+  }
+  return verify_impl(args, static_cast<cudaStream_t>(stream), nullptr, nullptr, 0, shards);
+}
+
+int es_shard_signal(uint64_t* flag, uint64_t epoch, void* stream) {
+  g_error.clear();
+  if (flag == nullptr) return fail(ES_ERR_ARGUMENT, "null flag");
+  if (const int dev = device_check(); dev != ES_SUCCESS) return dev;
+  cudaGetLastError();
+  es::signal_flag<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(flag, epoch);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? ES_SUCCESS : fail(ES_ERR_LAUNCH, std::string("flag launch failed: ") + cudaGetErrorString(e));
+}
+
+int es_shard_wait(const uint64_t* const* flags, int32_t count, uint64_t epoch, uint32_t* timeouts, void* stream) {
+  g_error.clear();
+  if (flags == nullptr || count < 1 || count > es::MAX_SHARDS) return fail(ES_ERR_ARGUMENT, "flags: 1 to 8 flags");
+  es::FlagSet f{};
+  for (int g = 0; g < count; ++g) {
+    if (flags[g] == nullptr) return fail(ES_ERR_ARGUMENT, "null flag");
+    f.flag[g] = flags[g];
+  }
+  f.count = count;
+  f.epoch = epoch;
+  f.timeouts = timeouts;
+  if (const int dev = device_check(); dev != ES_SUCCESS) return dev;
+  cudaGetLastError();
+  es::wait_flags<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(f);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? ES_SUCCESS : fail(ES_ERR_LAUNCH, std::string("wait launch failed: ") + cudaGetErrorString(e));
+}
+
+int es_ipc_alloc(uint64_t bytes, void** ptr, void* handle) {
+  g_error.clear();
+  if (ptr == nullptr || handle == nullptr || bytes == 0) return fail(ES_ERR_ARGUMENT, "invalid allocation request");
+  if (const int dev = device_check(); dev != ES_SUCCESS) return dev;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    if (p != nullptr) cudaFree(p);
+    return fail(ES_ERR_DEVICE, std::string("shared allocation failed: ") + cudaGetErrorString(e));
+  }
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  std::memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return ES_SUCCESS;
+}
+
+int es_ipc_open(const void* handle, void** ptr) {
+  g_error.clear();
+  if (ptr == nullptr || handle == nullptr) return fail(ES_ERR_ARGUMENT, "invalid handle");
+  if (const int dev = device_check(); dev != ES_SUCCESS) return dev;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? ES_SUCCESS : fail(ES_ERR_DEVICE, std::string("opening a peer's allocation failed: ") + cudaGetErrorString(e));
+}
+
+int es_ipc_close(void* ptr) {
+  g_error.clear();
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? ES_SUCCESS : fail(ES_ERR_DEVICE, cudaGetErrorString(e));
+}
+
+int es_ipc_free(void* ptr) {
+  g_error.clear();
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? ES_SUCCESS : fail(ES_ERR_DEVICE, cudaGetErrorString(e));
 }
 
 const char* es_last_error(void) { return g_error.c_str(); }

@@ -294,6 +294,17 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       "l"(src), "r"(bytes), "r"(smem_addr(bar))
       : "memory");
 }
+// Flags shared between GPUs (vocabulary-sharded calls): a system-scope
+// release store and acquire load of a 64-bit word in global memory (a peer
+// GPU's memory for the loads).
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 // Programmatic dependent launch: the row kernel starts its loads while the
 // preparation kernel runs, and waits for it before reading what it wrote.
 __device__ __forceinline__ void wait_for_prerequisite_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

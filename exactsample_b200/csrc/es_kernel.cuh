@@ -4,8 +4,8 @@
 
 namespace es {
 
-constexpr uint32_t BULK_CHUNK = 16384;  // bytes per TMA bulk copy
 constexpr uint32_t WAIT_LIMIT = 1u << 22;  // mbarrier polls (about a second) before a copy is declared lost
+constexpr uint32_t PEER_WAIT_LIMIT = 1u << 20;  // polls of a peer GPU's flag (about a second) before giving up
 
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
@@ -310,13 +310,32 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_
   // 1. Start copying this rank's slice (and mask words) before waiting for
   //    the preparation kernel: they are inputs, which it never writes.
   //    Resident rows copy the whole slice; streamed rows fill the TMA ring.
+  bool lost = false;  // a bounded wait gave up: the row is not trusted
   if (threadIdx.x == 0) {
     mbar_init(&s.bar, 1);
     for (int i = 0; i < MAX_RING_STAGES; ++i) mbar_init(&s.ring_bar[i], 1);
     mbar_init_fence();
+    s.timeout = 0;
+    if (r.sharded) {
+      // A vocabulary-sharded call: only rows of this GPU's requests, and
+      // only once every GPU has written its shard (offsets are an input:
+      // malformed ones are caught by the preparation kernel).
+      const int req = request_of(p, r.row);
+      s.ctx.skip = req < p.sh.req_begin || req >= p.sh.req_end;
+      if (!s.ctx.skip)
+        for (int g = 0; g < p.sh.count; ++g)
+          for (uint32_t spins = 0; ld_acquire_sys(p.sh.ready[g]) < p.sh.epoch;)
+            if (++spins >= PEER_WAIT_LIMIT) {
+              s.timeout = 1;
+              break;
+            }
+    }
   }
   __syncthreads();
-  const T* src = static_cast<const T*>(p.target) + int64_t(r.row) * p.t_s0;
+  if (r.sharded) {
+    if (s.ctx.skip) return;  // the same on every rank of the cluster
+    lost = s.timeout != 0;
+  }
   const int n = r.hi - r.lo;
   if (stream) {
     if (threadIdx.x == 0) {
@@ -328,14 +347,12 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_
     const uint32_t bytes = uint32_t(n) * uint32_t(sizeof(T)), bulk = bytes & ~15u;
     if (threadIdx.x == 0) {
       mbar_arrive_expect_tx(&s.bar, bulk);
-      const uint8_t* from = reinterpret_cast<const uint8_t*>(src + r.lo);
-      for (uint32_t off = 0; off < bulk; off += BULK_CHUNK)
-        bulk_load(reinterpret_cast<uint8_t*>(slice) + off, from + off, min(BULK_CHUNK, bulk - off), &s.bar);
+      r.bulk_columns(slice, r.lo, int(bulk / sizeof(T)), &s.bar);
     }
-    for (int i = int(bulk / sizeof(T)) + threadIdx.x; i < n; i += THREADS) slice[i] = src[r.lo + i];
+    for (int i = int(bulk / sizeof(T)) + threadIdx.x; i < n; i += THREADS) slice[i] = *r.target_at(r.lo + i);
   } else {
     if (threadIdx.x == 0) mbar_arrive_expect_tx(&s.bar, 0);
-    for (int i = threadIdx.x; i < n; i += THREADS) slice[i] = src[int64_t(r.lo + i) * p.t_s1];
+    for (int i = threadIdx.x; i < n; i += THREADS) slice[i] = *r.target_at(r.lo + i);
   }
   if (!stream && p.mask != nullptr)
     for (int w = threadIdx.x; w < (n + 31) / 32; w += THREADS)
@@ -344,7 +361,6 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_
   // 2. The preparation kernel's statuses and counters, then the copy.
   wait_for_prerequisite_grid();
   ES_TRACE(p.workspace, p.rows, r.row, r.rank, 1);
-  bool lost = false;
   for (uint32_t spins = 0; !mbar_try_wait(&s.bar, 0);)
     if (++spins >= WAIT_LIMIT) {
       lost = true;

@@ -12,6 +12,27 @@ constexpr int DIST_BINS = 128;  // distance-below-maximum bins of 0.5 logit, plu
 constexpr int RADIX = 256;      // digits per radix-select level
 constexpr int MAX_RING_STAGES = 4;     // streamed rows: deepest TMA ring
 constexpr uint32_t RING_CHUNK = 16384; // bytes per ring stage (a multiple of 32 tokens of any dtype)
+constexpr uint32_t BULK_CHUNK = 16384; // bytes per TMA bulk copy
+
+// Vocabulary-sharded calls: the row's columns live on `count` GPUs, shard g
+// holding columns [g * cols, min(vocab, (g + 1) * cols)) in a buffer every
+// GPU can read (the same layout on each: the target strides of Params). This
+// GPU finishes requests [req_begin, req_end) and writes their outputs into
+// every GPU's output buffers. count <= 1: not sharded.
+constexpr int MAX_SHARDS = 8;
+struct Shards {
+  int32_t count, rank, cols;
+  int32_t req_begin, req_end;
+  int32_t pad;
+  uint64_t epoch;                   // this call's number, the same on every GPU
+  const void* target[MAX_SHARDS];
+  const void* draft[MAX_SHARDS];
+  int64_t* tokens[MAX_SHARDS];
+  int32_t* accepted[MAX_SHARDS];
+  int32_t* status[MAX_SHARDS];
+  int32_t* path[MAX_SHARDS];
+  const uint64_t* ready[MAX_SHARDS];  // each GPU's "shard written" flag (>= epoch once written)
+};
 
 // Kernel arguments (filled by es_verify from es_args); strides in elements.
 struct Params {
@@ -57,7 +78,19 @@ struct Params {
   int32_t offsets_inline;  // the preparation kernel validates cu_rows itself
   int32_t exact_draws;     // dispatch="reference": every draw scored in FP64, no lists
   int32_t stream_rows;     // 0: rows stay in shared memory; else the depth (2..4) of the TMA ring they stream through
+  Shards sh;
 };
+
+// One GPU's output buffers (the caller's, or shard g's in a sharded call).
+struct Outputs {
+  int64_t* tokens;
+  int32_t *accepted, *status, *path;
+};
+__device__ __forceinline__ int output_sets(const Params& p) { return p.sh.count > 1 ? p.sh.count : 1; }
+__device__ __forceinline__ Outputs output_set(const Params& p, int i) {
+  if (p.sh.count > 1) return Outputs{p.sh.tokens[i], p.sh.accepted[i], p.sh.status[i], p.sh.path[i]};
+  return Outputs{p.tokens, p.accepted, p.status, p.path};
+}
 
 // Per-row outcome, written by the row's cluster rank 0 and read by whichever
 // row of the request finishes last.

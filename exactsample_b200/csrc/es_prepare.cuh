@@ -60,37 +60,45 @@ __device__ inline int32_t metadata_status(const Params& p, int64_t req) {
 //     impossible zero-residual rejection is an error, not an EOS).
 __device__ inline void finish_request(const Params& p, int64_t req, int begin, int end) {
   const RowResult* results = row_results(p.workspace);
-  int32_t* status = &p.status[req * p.st_s];
-  for (int pass = 0; pass < 2; ++pass)
+  // The outcome: a failed status, or `accepted` drafts followed by `last`.
+  int32_t failed = ES_OK;
+  for (int pass = 0; pass < 2 && failed == ES_OK; ++pass)
     for (int row = begin; row < end; ++row) {
       const int32_t s = pass == 0 ? __ldcg(&results[row].target_status) : __ldcg(&results[row].status);
       if (s != ES_OK) {
-        *status = s;
-        return;
+        failed = s;
+        break;
       }
     }
-  int64_t* tokens = p.tokens + req * p.tok_s0;
   const int drafts = end - begin - 1;
-  for (int i = 0; i < drafts; ++i) {
-    const int row = begin + i;
-    const int64_t draft = p.draft_ids[req * p.d_s0 + int64_t(i) * p.d_s1];
-    const int32_t sample = __ldcg(&results[row].sample);
-    const bool accept = p.mode == ES_COUPLED ? sample == draft : __ldcg(&results[row].accept) != 0;
-    if (!accept) {
-      const int32_t token = p.mode == ES_COUPLED ? sample : __ldcg(&results[row].residual);
-      if (token < 0) {
-        *status = ES_INVALID_INPUT;
-        return;
+  int accepted = drafts;
+  int64_t last = -1;
+  if (failed == ES_OK) {
+    for (int i = 0; i < drafts; ++i) {
+      const int row = begin + i;
+      const int64_t draft = p.draft_ids[req * p.d_s0 + int64_t(i) * p.d_s1];
+      const int32_t sample = __ldcg(&results[row].sample);
+      const bool accept = p.mode == ES_COUPLED ? sample == draft : __ldcg(&results[row].accept) != 0;
+      if (!accept) {
+        accepted = i;
+        last = p.mode == ES_COUPLED ? sample : __ldcg(&results[row].residual);
+        if (last < 0) failed = ES_INVALID_INPUT;
+        break;
       }
-      for (int j = 0; j < i; ++j) tokens[j * p.tok_s1] = p.draft_ids[req * p.d_s0 + int64_t(j) * p.d_s1];
-      tokens[i * p.tok_s1] = token;
-      p.accepted[req * p.acc_s] = i;
-      return;
     }
+    if (accepted == drafts) last = __ldcg(&results[end - 1].sample);
   }
-  for (int j = 0; j < drafts; ++j) tokens[j * p.tok_s1] = p.draft_ids[req * p.d_s0 + int64_t(j) * p.d_s1];
-  tokens[drafts * p.tok_s1] = __ldcg(&results[end - 1].sample);
-  p.accepted[req * p.acc_s] = drafts;
+  for (int set = 0; set < output_sets(p); ++set) {
+    const Outputs o = output_set(p, set);
+    if (failed != ES_OK) {
+      o.status[req * p.st_s] = failed;
+      continue;
+    }
+    int64_t* tokens = o.tokens + req * p.tok_s0;
+    for (int j = 0; j < accepted; ++j) tokens[j * p.tok_s1] = p.draft_ids[req * p.d_s0 + int64_t(j) * p.d_s1];
+    tokens[accepted * p.tok_s1] = last;
+    o.accepted[req * p.acc_s] = accepted;
+  }
 }
 
 }  // namespace es

@@ -205,9 +205,8 @@ template <int DT> struct Row {
   uint32_t* mask_s;  // this rank's mask words (resident rows)
   W* tmax;           // per 32-token tile of the slice: the largest valid value (-inf if none)
   T* slice;          // this rank's logits (resident rows) or the TMA ring (streamed rows)
-  const T* grow;     // the slice in global memory
-  int64_t gs;        // its element stride
-  bool resident, vec;
+  const T* tbase;    // the row in global memory (not sharded)
+  bool resident, vec, sharded;
   cg::cluster_group cluster;
   int rank, ranks, row, lo, hi, groups;
   int xc;  // exchanges so far (the same on every rank)
@@ -234,8 +233,38 @@ template <int DT> struct Row {
     has_mask = p.mask != nullptr;
     resident = !p.stream_rows;
     vec = p.vector_load != 0;
-    gs = p.t_s1;
-    grow = static_cast<const T*>(p.target) + int64_t(row) * p.t_s0 + int64_t(lo) * p.t_s1;
+    sharded = p.sh.count > 1;
+    tbase = static_cast<const T*>(p.target) + int64_t(row) * p.t_s0;
+  }
+
+  // ---- global memory ----
+  // Column t of the row's target and proposal logits: in the caller's
+  // tensors, or in shard t / cols of a vocabulary-sharded call (a peer GPU's
+  // buffer for most columns).
+  __device__ __forceinline__ const T* target_at(int t) const {
+    if (!sharded) return tbase + int64_t(t) * p.t_s1;
+    const int g = t / p.sh.cols;
+    return static_cast<const T*>(p.sh.target[g]) + int64_t(row) * p.t_s0 + int64_t(t - g * p.sh.cols) * p.t_s1;
+  }
+  __device__ __forceinline__ const T* draft_at(int t) const {
+    if (!sharded) return static_cast<const T*>(p.draft) + int64_t(row) * p.q_s0 + int64_t(t) * p.q_s1;
+    const int g = t / p.sh.cols;
+    return static_cast<const T*>(p.sh.draft[g]) + int64_t(row) * p.q_s0 + int64_t(t - g * p.sh.cols) * p.q_s1;
+  }
+  // TMA bulk copies of columns [c0, c0 + n) of the target row into dst
+  // (16-byte aligned, n * sizeof(T) a multiple of 16), in pieces of at most
+  // BULK_CHUNK bytes that never cross a shard boundary (shard widths are
+  // multiples of 16 columns), all completing on `bar`.
+  __device__ void bulk_columns(void* dst, int c0, int n, uint64_t* bar) const {
+    uint8_t* d = static_cast<uint8_t*>(dst);
+    while (n > 0) {
+      int piece = min(n, int(BULK_CHUNK / sizeof(T)));
+      if (sharded) piece = min(piece, (c0 / p.sh.cols + 1) * p.sh.cols - c0);
+      bulk_load(d, target_at(c0), uint32_t(piece) * uint32_t(sizeof(T)), bar);
+      d += size_t(piece) * sizeof(T);
+      c0 += piece;
+      n -= piece;
+    }
   }
 
   // ---- slice access ----
@@ -258,12 +287,12 @@ template <int DT> struct Row {
     if (resident) {
       load4(slice + 4 * g, v);
     } else if (vec && 4 * g + 4 <= hi - lo) {
-      load4_global(grow + 4 * g, v);
+      load4_global(target_at(lo + 4 * g), v);  // four columns never straddle a shard boundary
     } else {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int t = 4 * g + j;
-        v[j] = t < hi - lo ? widen(grow[int64_t(t) * gs]) : W(-INFINITY);
+        v[j] = t < hi - lo ? widen(*target_at(lo + t)) : W(-INFINITY);
       }
     }
   }
@@ -279,7 +308,7 @@ template <int DT> struct Row {
   }
   // A single token anywhere in the row, from global memory.
   __device__ __forceinline__ W value_global(int t) const {
-    return widen(static_cast<const T*>(p.target)[int64_t(row) * p.t_s0 + int64_t(t) * p.t_s1]);
+    return widen(*target_at(t));
   }
   __device__ __forceinline__ bool allowed_global(int t) const {
     return !has_mask || ((uint32_t(p.mask[int64_t(row) * p.m_s0 + int64_t(t >> 5) * p.m_s1]) >> (t & 31)) & 1u);
@@ -288,7 +317,7 @@ template <int DT> struct Row {
     return allowed_global(t) && value_global(t) > W(-INFINITY);
   }
   __device__ __forceinline__ W q_value(int t) const {
-    return widen(static_cast<const T*>(p.draft)[int64_t(row) * p.q_s0 + int64_t(t) * p.q_s1]);
+    return widen(*draft_at(t));
   }
 
   // ---- cluster exchange ----
@@ -416,7 +445,7 @@ template <int DT> struct Row {
   // Local token i of the slice (0 <= i < hi - lo): its value and whether the
   // mask allows it.
   __device__ __forceinline__ W value_local(int i) const {
-    return resident ? widen(slice[i]) : widen(grow[int64_t(i) * gs]);
+    return resident ? widen(slice[i]) : widen(*target_at(lo + i));
   }
   __device__ __forceinline__ bool allowed_local(int i) const {
     if (!has_mask) return true;
@@ -461,8 +490,8 @@ template <int DT> struct Row {
     const int stage = c % p.stream_rows;
     uint64_t* bar = &s.ring_bar[stage];
     mbar_arrive_expect_tx(bar, len);
-    bulk_load(reinterpret_cast<uint8_t*>(slice) + stage * RING_CHUNK,
-              reinterpret_cast<const uint8_t*>(grow) + off, len, bar);
+    bulk_columns(reinterpret_cast<uint8_t*>(slice) + stage * RING_CHUNK, lo + int(off / sizeof(T)),
+                 int(len / sizeof(T)), bar);
   }
   // The statistics pass over the whole slice: from shared memory (resident),
   // through the TMA ring (streamed, 16-byte aligned rows), or from global

@@ -137,6 +137,63 @@ int es_verify_timed(const es_args* args, void* stream, void* before, void* after
 #define ES_STATIC_MAX_ROWS 4096
 int es_verify_static(const es_args* args, void* stream);
 
+/* ---- Vocabulary-sharded calls (no counterpart in the reference) ----
+ *
+ * N GPUs (2..8, one process each) hold contiguous shards of the vocabulary of
+ * every row: shard g holds columns [g * cols, min(vocab, (g + 1) * cols)),
+ * cols a multiple of 16, in a buffer every GPU can read (es_ipc_alloc on its
+ * owner, es_ipc_open on the others). All other inputs are replicated. Each
+ * GPU finishes the requests [req_begin, req_end), streaming their full rows
+ * (its own shard from HBM, the others' over NVLink with TMA bulk copies), and
+ * writes their outputs into every GPU's output buffers, which must therefore
+ * be registered buffers too. Results are identical to an unsharded call.
+ *
+ * One call on each GPU, all with the same arguments and epoch (a call
+ * number, increasing from 1), in this order on the GPU's stream:
+ *   es_shard_signal(ready[rank], epoch)    after this GPU's shard is written;
+ *   es_verify_sharded(args, shards)        waits for every ready flag first;
+ *   es_shard_signal(done[rank], epoch);
+ *   es_shard_wait(done, count, epoch)      afterwards every GPU's outputs are
+ *                                          complete and no GPU reads this
+ *                                          GPU's shard any more.
+ * Every wait is bounded (about a second): a wait that gives up marks the
+ * affected rows INVALID_INPUT (es_verify_sharded) or adds one to *timeouts
+ * (es_shard_wait). */
+#define ES_MAX_SHARDS 8
+typedef struct es_shards {
+  int32_t count;          /* GPUs holding shards, 2..ES_MAX_SHARDS */
+  int32_t rank;           /* this GPU's shard */
+  int64_t cols;           /* columns per shard (the last holds the rest) */
+  int64_t vocab;          /* columns of the whole row */
+  int64_t req_begin;      /* requests this GPU finishes: [req_begin, req_end) */
+  int64_t req_end;
+  uint64_t epoch;         /* this call's number, the same on every GPU */
+  const void* target[ES_MAX_SHARDS];  /* every GPU's target shard buffer; [rank] is args->target_logits */
+  const void* draft[ES_MAX_SHARDS];   /* every GPU's draft shard buffer (full-q drafts), else NULL */
+  void* tokens[ES_MAX_SHARDS];        /* every GPU's outputs, laid out as args' outputs */
+  void* accepted[ES_MAX_SHARDS];
+  void* status[ES_MAX_SHARDS];
+  void* path[ES_MAX_SHARDS];
+  const uint64_t* ready[ES_MAX_SHARDS];  /* every GPU's "shard written" flag */
+} es_shards;
+
+/* es_verify for one GPU of a sharded call: args->target_logits (and
+ * draft_logits) are this GPU's shard [rows, its columns]; draft_ids, mask
+ * and the rest describe the whole rows (vocab = shards->vocab). */
+int es_verify_sharded(const es_args* args, const es_shards* shards, void* stream);
+/* Stores `epoch` into `flag` (this GPU's ready or done flag) once the
+ * stream's earlier work is done. */
+int es_shard_signal(uint64_t* flag, uint64_t epoch, void* stream);
+/* Waits on the stream until every flags[i] (i < count) has reached `epoch`. */
+int es_shard_wait(const uint64_t* const* flags, int32_t count, uint64_t epoch, uint32_t* timeouts, void* stream);
+/* Device memory other processes on this node can map: es_ipc_alloc returns a
+ * zeroed allocation and its 64-byte handle; es_ipc_open maps a handle made
+ * by another process (es_ipc_close unmaps it, es_ipc_free frees one's own). */
+int es_ipc_alloc(uint64_t bytes, void** ptr, void* handle);
+int es_ipc_open(const void* handle, void** ptr);
+int es_ipc_close(void* ptr);
+int es_ipc_free(void* ptr);
+
 /* The message of the last error returned on this thread ("" after success). */
 const char* es_last_error(void);
 
