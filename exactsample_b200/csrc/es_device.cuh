@@ -286,7 +286,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return done != 0;
 }
-// Global -> this CTA's shared memory bulk copy (TMA, no multicast). dst, src
+// Global -> this CTA's own shared memory bulk copy (TMA, one destination). dst, src
 // and bytes must be multiples of 16.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
