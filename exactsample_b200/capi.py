@@ -16,7 +16,7 @@ ERRORS = {0: "ES_SUCCESS", -1: "ES_ERR_ARGUMENT", -2: "ES_ERR_CAPACITY", -3: "ES
           -4: "ES_ERR_ALIAS", -5: "ES_ERR_UNSUPPORTED", -6: "ES_ERR_LAUNCH", -7: "ES_ERR_DEVICE"}
 # Every function the header declares.
 EXPORTS = ["es_workspace_bytes", "es_verify", "es_verify_timed", "es_verify_static", "es_verify_sharded",
-           "es_shard_signal", "es_shard_wait", "es_ipc_alloc", "es_ipc_open", "es_ipc_close", "es_ipc_free",
+           "es_shard_signal", "es_shard_wait", "es_shard_finish", "es_ipc_alloc", "es_ipc_open", "es_ipc_close", "es_ipc_free",
            "es_last_error", "es_abi_version"]
 MAX_SHARDS = 8  # ES_MAX_SHARDS
 STATIC_MAX_ROWS = 4096  # ES_STATIC_MAX_ROWS
@@ -74,6 +74,9 @@ def load(path: str | Path | None = None) -> ctypes.CDLL:
         lib.es_shard_wait.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, ctypes.c_uint64,
                                       ctypes.c_void_p, ctypes.c_void_p]
         lib.es_shard_wait.restype = ctypes.c_int
+        lib.es_shard_finish.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32,
+                                        ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]
+        lib.es_shard_finish.restype = ctypes.c_int
         lib.es_ipc_alloc.argtypes = [ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p]
         lib.es_ipc_alloc.restype = ctypes.c_int
         lib.es_ipc_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]

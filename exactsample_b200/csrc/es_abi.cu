@@ -25,6 +25,10 @@ __global__ void __launch_bounds__(1024) check_offsets(const __grid_constant__ Pa
 // accepted 0), metadata status, path, and the request's arrival counter.
 __global__ void __launch_bounds__(128) prepare(const __grid_constant__ Params p) {
   allow_dependent_grid();  // the row kernel may launch now and start loading logits
+  // A vocabulary-sharded call: the stream's earlier work (this GPU's shard)
+  // is done, so tell the peers.
+  if (p.sh.count > 1 && blockIdx.x == 0 && threadIdx.x == 0)
+    st_release_sys(const_cast<uint64_t*>(p.sh.ready[p.sh.rank]), p.sh.epoch);
   bool bad;
   if (p.offsets_inline) {
     bad = offsets_malformed(p);
@@ -95,7 +99,7 @@ struct FlagSet {
   uint64_t epoch;
   uint32_t* timeouts;
 };
-__global__ void wait_flags(const __grid_constant__ FlagSet f) {
+__device__ void wait_all(const FlagSet& f) {
   for (int g = 0; g < f.count; ++g)
     for (uint32_t spins = 0; ld_acquire_sys(f.flag[g]) < f.epoch;)
       if (++spins >= (1u << 20)) {
@@ -103,6 +107,13 @@ __global__ void wait_flags(const __grid_constant__ FlagSet f) {
         break;
       }
   __threadfence_system();
+}
+__global__ void wait_flags(const __grid_constant__ FlagSet f) { wait_all(f); }
+// The end of a sharded call on one GPU: its done flag, then every GPU's.
+__global__ void finish_flags(uint64_t* mine, const __grid_constant__ FlagSet f) {
+  __threadfence_system();
+  st_release_sys(mine, f.epoch);
+  wait_all(f);
 }
 
 template <int DT> cudaError_t launch_rows(const Params& p, int cluster, cudaStream_t stream);
@@ -569,6 +580,26 @@ int es_shard_wait(const uint64_t* const* flags, int32_t count, uint64_t epoch, u
   es::wait_flags<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(f);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? ES_SUCCESS : fail(ES_ERR_LAUNCH, std::string("wait launch failed: ") + cudaGetErrorString(e));
+}
+
+int es_shard_finish(uint64_t* done, const uint64_t* const* flags, int32_t count, uint64_t epoch, uint32_t* timeouts,
+                    void* stream) {
+  g_error.clear();
+  if (done == nullptr || flags == nullptr || count < 1 || count > es::MAX_SHARDS)
+    return fail(ES_ERR_ARGUMENT, "flags: this GPU's done flag and 1 to 8 flags");
+  es::FlagSet f{};
+  for (int g = 0; g < count; ++g) {
+    if (flags[g] == nullptr) return fail(ES_ERR_ARGUMENT, "null flag");
+    f.flag[g] = flags[g];
+  }
+  f.count = count;
+  f.epoch = epoch;
+  f.timeouts = timeouts;
+  if (const int dev = device_check(); dev != ES_SUCCESS) return dev;
+  cudaGetLastError();
+  es::finish_flags<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(done, f);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? ES_SUCCESS : fail(ES_ERR_LAUNCH, std::string("finish launch failed: ") + cudaGetErrorString(e));
 }
 
 int es_ipc_alloc(uint64_t bytes, void** ptr, void* handle) {

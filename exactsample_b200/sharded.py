@@ -172,7 +172,9 @@ class ShardedPlan:
         torch.cuda.synchronize(self.device)
         return int(self._timeouts.item())
 
-    # ---- the four steps of a call (verify_sharded runs them in order) ----
+    # ---- the steps of a call: verify_sharded runs launch then finish;
+    # several shards on one GPU need signal_ready, launch, signal_done and
+    # wait_done, each issued for every shard before the next ----
     def signal_ready(self, stream=None) -> None:
         capi.check(capi.load().es_shard_signal(ctypes.c_void_p(self._base), self.epoch, self._stream(stream)))
 
@@ -212,6 +214,13 @@ class ShardedPlan:
         capi.check(capi.load().es_shard_wait(ctypes.cast(flags, ctypes.POINTER(ctypes.c_void_p)), self.shards,
                                              self.epoch, ctypes.c_void_p(self._base + 128), self._stream(stream)))
 
+    def finish(self, stream=None) -> None:
+        """signal_done and wait_done as one launch."""
+        flags = self._ptrs("done")
+        capi.check(capi.load().es_shard_finish(ctypes.c_void_p(self._base + 64),
+                                               ctypes.cast(flags, ctypes.POINTER(ctypes.c_void_p)), self.shards,
+                                               self.epoch, ctypes.c_void_p(self._base + 128), self._stream(stream)))
+
     def _stream(self, stream):
         import torch
 
@@ -237,9 +246,7 @@ def verify_sharded(plan: ShardedPlan, rows: int, cu_rows, draft_ids, *, params: 
     """One GPU's part of a sharded call over plan.logits[:rows]; returns plan.out
     (complete for every request once the stream reaches the end of the call)."""
     plan.epoch += 1
-    plan.signal_ready()
     plan.launch(rows, cu_rows, draft_ids, params=params, rng=rng, mask=mask, mode=mode, dispatch=dispatch,
-                top_k_top_p=top_k_top_p)
-    plan.signal_done()
-    plan.wait_done()
+                top_k_top_p=top_k_top_p)  # raises this GPU's ready flag first
+    plan.finish()
     return plan.out

@@ -149,13 +149,20 @@ int es_verify_static(const es_args* args, void* stream);
  * be registered buffers too. Results are identical to an unsharded call.
  *
  * One call on each GPU, all with the same arguments and epoch (a call
- * number, increasing from 1), in this order on the GPU's stream:
- *   es_shard_signal(ready[rank], epoch)    after this GPU's shard is written;
- *   es_verify_sharded(args, shards)        waits for every ready flag first;
- *   es_shard_signal(done[rank], epoch);
- *   es_shard_wait(done, count, epoch)      afterwards every GPU's outputs are
- *                                          complete and no GPU reads this
- *                                          GPU's shard any more.
+ * number, increasing from 1), in this order on the GPU's stream, after this
+ * GPU's shard is written:
+ *   es_verify_sharded(args, shards)        raises this GPU's ready flag, and
+ *                                          waits for every GPU's before
+ *                                          reading a shard;
+ *   es_shard_finish(done[rank], done, count, epoch)
+ *                                          raises this GPU's done flag and
+ *                                          waits for every GPU's: afterwards
+ *                                          every GPU's outputs are complete
+ *                                          and no GPU reads this GPU's shard.
+ * es_shard_signal and es_shard_wait are the two halves of es_shard_finish
+ * (and es_shard_signal on the ready flag the first step of
+ * es_verify_sharded), for a caller that runs several shards on one GPU and
+ * must issue every shard's signal before any shard's wait.
  * Every wait is bounded (about a second): a wait that gives up marks the
  * affected rows INVALID_INPUT (es_verify_sharded) or adds one to *timeouts
  * (es_shard_wait). */
@@ -186,6 +193,9 @@ int es_verify_sharded(const es_args* args, const es_shards* shards, void* stream
 int es_shard_signal(uint64_t* flag, uint64_t epoch, void* stream);
 /* Waits on the stream until every flags[i] (i < count) has reached `epoch`. */
 int es_shard_wait(const uint64_t* const* flags, int32_t count, uint64_t epoch, uint32_t* timeouts, void* stream);
+/* es_shard_signal(done, epoch) then es_shard_wait(flags, ...), as one launch. */
+int es_shard_finish(uint64_t* done, const uint64_t* const* flags, int32_t count, uint64_t epoch, uint32_t* timeouts,
+                    void* stream);
 /* Device memory other processes on this node can map: es_ipc_alloc returns a
  * zeroed allocation and its 64-byte handle; es_ipc_open maps a handle made
  * by another process (es_ipc_close unmaps it, es_ipc_free frees one's own). */

@@ -102,5 +102,8 @@ def test_flag_and_ipc_entry_points_need_a_gpu():
     flags = (ctypes.c_void_p * 1)(ctypes.cast(flag, ctypes.c_void_p))
     assert lib.es_shard_wait(flags, 1, 1, None, None) == -7
     assert lib.es_shard_wait(flags, 0, 1, None, None) == -1
+    done = ctypes.cast(flag, ctypes.c_void_p)
+    assert lib.es_shard_finish(done, flags, 1, 1, None, None) == -7
+    assert lib.es_shard_finish(None, flags, 1, 1, None, None) == -1
     ptr, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
     assert lib.es_ipc_alloc(1024, ctypes.byref(ptr), handle) == -7
