@@ -192,11 +192,11 @@ bool is_logit_dtype(int32_t d) { return d == ES_F32 || d == ES_F64 || d == ES_F1
 //     row's cluster fits on the GPU at once (small batches), with as many
 //     ranks per row as that allows (up to 16) to spread a row over SMs.
 //   * Streamed rows: each rank streams its slice through a TMA ring and later
-//     passes re-read global memory (L2); about two ranks per SM in all (one
-//     rank per row from 296 rows on), since one rank streams a row at well
+//     passes re-read global memory (L2); about three ranks per SM in all (one
+//     rank per row from 444 rows on), since one rank streams a row at well
 //     under an SM's share of HBM bandwidth.
 constexpr size_t RESIDENT_BYTES = 80 * 1024;
-constexpr int SM_COUNT = 148, RESIDENT_SLOTS = 2 * SM_COUNT;
+constexpr int SM_COUNT = 148, RESIDENT_SLOTS = 2 * SM_COUNT, STREAM_SLOTS = 3 * SM_COUNT;
 constexpr size_t MAX_SMEM = 227 * 1024;
 
 template <int DT> size_t smem_for(int sw, int stages) { return es::smem_bytes<DT>(sw, stages); }
@@ -221,7 +221,7 @@ int choose_cluster(int64_t rows, int64_t vocab, int dtype, int* slice_words, siz
     if (vocab < 4096) c = resident_min;  // tiny rows: one rank
   } else {
     streamed = true;
-    c = int(std::min<int64_t>(16, std::max<int64_t>(1, RESIDENT_SLOTS / std::max<int64_t>(rows, 1))));
+    c = int(std::min<int64_t>(16, std::max<int64_t>(1, STREAM_SLOTS / std::max<int64_t>(rows, 1))));
   }
   // EXACTSAMPLE_CLUSTER=n asks for n ranks per row (1..16), e.g. to show that
   // results do not depend on the split; EXACTSAMPLE_STREAM=0/1 forces the row
@@ -236,7 +236,8 @@ int choose_cluster(int64_t rows, int64_t vocab, int dtype, int* slice_words, siz
   }
   // The TMA ring: four 16 KB stages while every rank has a place on the GPU
   // with two per SM; two stages beyond that, so that three ranks fit an SM
-  // (EXACTSAMPLE_RING=2..4 forces the depth).
+  // (the kernel is then compiled for three blocks per SM; EXACTSAMPLE_RING=2..4
+  // forces the depth).
   int stages = 0;
   if (streamed) {
     stages = rows * c > RESIDENT_SLOTS ? 2 : es::MAX_RING_STAGES;

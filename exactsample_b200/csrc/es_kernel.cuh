@@ -78,6 +78,12 @@ template <int DT> struct RowKernel {
     const int i = lane_id();
     const bool in = i < n_keep;
     const int id = in ? r.s.u.cand.id[i] : INT_MAX;
+    // The lane's Gumbel noise for the one draw this row can need (substream
+    // 2 for a ratio test's residual, else 0), computed first so that it
+    // overlaps the weight and prefix chain below.
+    const uint32_t draw_sub = verify && !full_q ? 2u : 0u;
+    const double noise = in ? noise64(r.addr.word(draw_sub, uint32_t(id))) : 0.0;
+    ES_TRACE(r.p.workspace, r.p.rows, r.row, r.rank, 11);
     double w = 0;
     bool ok = false;
     if (in) {
@@ -119,15 +125,18 @@ template <int DT> struct RowKernel {
       r.count_near_tie(near);
     }
     const double prob = i < n2 ? w / denominator : 0.0;
+    ES_TRACE(r.p.workspace, r.p.rows, r.row, r.rank, 12);
     // One draw over the list: argmax log(p) + G, lowest ID on ties.
     auto draw_list = [&](uint32_t sub, int excluded) {
       Best b = no_best();
-      if (i < n2 && id != excluded && prob > 0) b = Best{log(prob) + noise64(r.addr.word(sub, uint32_t(id))), id};
+      if (i < n2 && id != excluded && prob > 0)
+        b = Best{log(prob) + (sub == draw_sub ? noise : noise64(r.addr.word(sub, uint32_t(id)))), id};
       b = warp_all(b, [](Best a, Best c2) { return best_of(a, c2); });
       return b.id == INT_MAX ? -1 : b.id;
     };
     if (!verify) {
       res.sample = draw_list(0, -1);
+      ES_TRACE(r.p.workspace, r.p.rows, r.row, r.rank, 15);
       return;
     }
     const unsigned at_draft = __ballot_sync(ALL, i < n2 && id == c.draft_id);

@@ -788,42 +788,69 @@ template <int DT> struct Row {
       }
     }
     __syncthreads();
+    ES_TRACE(p.workspace, p.rows, row, rank, 13);
     const int listed = s.n_tiles;
     int* counter = peer(&s.n_cand, 0);
     uint64_t* keys = peer(s.u.cand.key, 0);
     int32_t* ids = peer(s.u.cand.id, 0);
     int mine = 0;  // tokens this warp gathered (the same in every lane)
-    // One tile, read by the whole warp (warp-uniform call).
-    auto take_tile = [&](int t) {
+    // Token lane of tile t: its value, -inf if it is past the slice or masked.
+    auto load_tile = [&](int t) {
       const int i = 32 * t + lane_id();
-      bool hit = false;
-      W v = W(-INFINITY);
-      if (i < hi - lo) {
-        v = value_local(i);
-        hit = allowed_local(i) && v > W(-INFINITY) && dist_bin(v) <= window;
+      return i < hi - lo && allowed_local(i) ? value_local(i) : W(-INFINITY);
+    };
+    // Tiles' tokens within the window, appended by the whole warp
+    // (warp-uniform call; t[b] < 0 marks no tile): one atomic on rank 0's
+    // counter reserves the slots of all of them.
+    auto take_tiles = [&](const int* t, const W* v, int count) {
+      unsigned hits[4];
+      int total = 0;
+      for (int b = 0; b < count; ++b) {
+        const bool hit = t[b] >= 0 && v[b] > W(-INFINITY) && dist_bin(v[b]) <= window;
+        hits[b] = __ballot_sync(0xffffffffu, hit);
+        total += __popc(hits[b]);
       }
-      const unsigned b = __ballot_sync(0xffffffffu, hit);
-      if (b == 0) return;
+      if (total == 0) return;
       int base = 0;
-      if (lane_id() == 0) base = atomicAdd(counter, __popc(b));
+      if (lane_id() == 0) base = atomicAdd(counter, total);
       base = __shfl_sync(0xffffffffu, base, 0);
-      if (hit) {
-        const int at_ = base + __popc(b & ((1u << lane_id()) - 1u));
-        if (at_ < CAP) {
-          keys[at_] = uint64_t(order_key(v));
-          ids[at_] = lo + i;
+      for (int b = 0; b < count; ++b) {
+        if ((hits[b] >> lane_id()) & 1u) {
+          const int at_ = base + __popc(hits[b] & ((1u << lane_id()) - 1u));
+          if (at_ < CAP) {
+            keys[at_] = uint64_t(order_key(v[b]));
+            ids[at_] = lo + 32 * t[b] + lane_id();
+          }
         }
+        base += __popc(hits[b]);
       }
-      mine += __popc(b);
+      mine += total;
     };
     if (listed <= TILE_CAP) {
-      for (int k = warp_id(); k < listed; k += WARPS) take_tile(s.tiles[k]);
+      // A warp's listed tiles in batches: all of a batch's loads (L2 for
+      // streamed rows) are in flight before the first is used.
+      constexpr int BATCH = 4;
+      for (int k0 = warp_id(); k0 < listed; k0 += WARPS * BATCH) {
+        W v[BATCH];
+        int t[BATCH];
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b) {
+          const int k = k0 + b * WARPS;
+          t[b] = k < listed ? s.tiles[k] : -1;
+          v[b] = t[b] >= 0 ? load_tile(t[b]) : W(-INFINITY);
+        }
+        take_tiles(t, v, BATCH);
+      }
     } else {  // too many tiles to list: every warp walks the tile maxima
       for (int t = warp_id(); t < nt; t += WARPS) {
         const W m = tmax[t];
-        if (m > W(-INFINITY) && dist_bin(m) <= window) take_tile(t);
+        if (m > W(-INFINITY) && dist_bin(m) <= window) {
+          const W v = load_tile(t);
+          take_tiles(&t, &v, 1);
+        }
       }
     }
+    ES_TRACE(p.workspace, p.rows, row, rank, 14);
     mine = block_all(lane_id() == 0 ? mine : 0, [](int x, int y) { return x + y; }, s.red.ints);
     if (int(threadIdx.x) < ranks) peer(s.pushed, threadIdx.x)[rank] = mine;
     exchange();
