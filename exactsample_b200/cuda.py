@@ -90,9 +90,11 @@ class _Ownership:
         self.event.record(torch.cuda.current_stream(device))
         self.event.synchronize()
 
-    def claim(self, stream) -> None:
+    def claim(self, stream, capturing: bool = False) -> None:
         if not self.lock.acquire(blocking=False):
             raise RuntimeError("exactsample workspace is already in use by another host call")
+        if capturing:  # events cannot be queried inside a capture
+            return
         if self.stream is not None and self.stream != stream.cuda_stream and not self.event.query():
             self.lock.release()
             raise RuntimeError("exactsample workspace is in flight on another stream; synchronize or use a separate plan")
@@ -121,11 +123,21 @@ class CudaPlan:
 
     Inputs and outputs must not be mutated until ``synchronize`` or normal CUDA
     stream ordering establishes completion. Tensor allocator lifetimes are
-    recorded on the consuming stream. CUDA graph capture is not supported.
+    recorded on the consuming stream.
+
+    CUDA graph capture is refused, as in the reference, unless the plan is
+    made with ``graphs=True``: ``verify`` then may be captured (it allocates
+    nothing and never synchronizes; its kernels and their programmatic
+    dependency are recorded as graph nodes). A captured call reads and writes
+    the tensors it was captured with, so a replay takes its inputs from those
+    same tensors; the ownership checks between streams are skipped during
+    capture, and replays of a plan's graphs must not overlap each other or
+    eager calls on the plan.
     """
 
     def __init__(self, max_rows: int, max_requests: int, max_draft: int, vocab: int,
-                 *, device: Any = "cuda", caps: dict | None = None, reference: bool = False):
+                 *, device: Any = "cuda", caps: dict | None = None, reference: bool = False,
+                 graphs: bool = False):
         import torch
 
         if caps:
@@ -140,6 +152,7 @@ class CudaPlan:
         # Kept sets of at most this many tokens are finished as an exact FP64
         # list; 0 sends every row to the full-row path (results are the same).
         self.list_max = 256
+        self.graphs = graphs
         self.device = torch.device("cuda", torch.cuda.current_device() if device.index is None else device.index)
         self.reference = reference
         # The reference's sizing, so plans are interchangeable: 8 bytes of
@@ -170,8 +183,10 @@ class CudaPlan:
 
 
 def plan(max_rows: int, max_requests: int, max_draft: int, vocab: int,
-         caps: dict | None = None, *, device: Any = "cuda", reference: bool = False) -> CudaPlan:
-    return CudaPlan(max_rows, max_requests, max_draft, vocab, device=device, caps=caps, reference=reference)
+         caps: dict | None = None, *, device: Any = "cuda", reference: bool = False,
+         graphs: bool = False) -> CudaPlan:
+    return CudaPlan(max_rows, max_requests, max_draft, vocab, device=device, caps=caps, reference=reference,
+                    graphs=graphs)
 
 
 def _check_call(target_logits, cu_rows, params, rng, plan: CudaPlan, mode: str, dispatch: str) -> int:
@@ -218,11 +233,12 @@ def verify(target_logits, cu_rows, draft_ids, *, params: CudaRequestParams,
                params.min_p, params.draft_kind, rng.seed, rng.stream_id, rng.positions, mask, plan.workspace,
                out.tokens, out.accepted_len, out.status, out.path_used)
     with torch.cuda.device(plan.device):
-        if torch.cuda.is_current_stream_capturing():
+        capturing = torch.cuda.is_current_stream_capturing()
+        if capturing and not plan.graphs:
             raise RuntimeError("exactsample v1 does not support CUDA graph capture")
         stream = torch.cuda.current_stream(plan.device)
         owner = plan._owner
-        owner.claim(stream)
+        owner.claim(stream, capturing)
         try:
             if any(t is not None and not isinstance(t, torch.Tensor) for t in tensors):
                 raise TypeError("all CUDA arguments must be preallocated tensors")
@@ -232,8 +248,10 @@ def verify(target_logits, cu_rows, draft_ids, *, params: CudaRequestParams,
             try:
                 torch.ops.exactsample.verify_out(*tensors, _MODES[mode], _DISPATCH[dispatch], plan.max_draft, list_max)
             finally:
-                # Even a failed launch may have enqueued work: keep ownership.
-                owner.enqueued(stream, [t for t in tensors if t is not None and t.device == plan.device])
+                # Even a failed launch may have enqueued work: keep ownership
+                # (a captured call enqueues nothing until its graph replays).
+                if not capturing:
+                    owner.enqueued(stream, [t for t in tensors if t is not None and t.device == plan.device])
             out.num_requests = requests
         finally:
             owner.release()

@@ -121,3 +121,49 @@ def test_fallback_counter_reads_zero_on_plain_rows():
     out, work = run_api(case)
     assert work.fallbacks() == 0
     assert (out.status[:8].cpu().numpy() == 0).all()
+
+
+def test_capture_is_refused_by_default_and_replays_exactly_with_graphs():
+    """The reference refuses graph capture (cuda.py:166-167); a plan made with
+    graphs=True allows it, and replays of the captured call give what eager
+    calls give on the same inputs, call after call."""
+    import torch
+    from exactsample_b200.cuda import CudaRequestParams, CudaRngKey, plan, verify
+    cases = [C.workload_case("C2a", requests=range(8), master_seed=s) for s in (21, 22, 23)]
+    t = device_inputs(cases[0])
+    rows, vocab = cases[0]["logits"].shape
+    requests = len(cases[0]["cu_rows"]) - 1
+    params = CudaRequestParams(t["temperature"], t["top_k"], t["top_p"], t["min_p"], t["draft_kind"])
+    rng = CudaRngKey(t["seeds"], t["stream_ids"], t["positions"])
+
+    def call(work, out):
+        verify(t["target_logits"], t["cu_rows"], t["draft_ids"], params=params, rng=rng, plan=work, out=out)
+
+    refusing = plan(rows, requests, t["_max_draft"], vocab)
+    refused_out = refusing.allocate_output()
+    graph = torch.cuda.CUDAGraph()
+    with pytest.raises(RuntimeError, match="graph capture"):
+        with torch.cuda.graph(graph):
+            call(refusing, refused_out)
+    torch.cuda.synchronize()
+
+    captured = plan(rows, requests, t["_max_draft"], vocab, graphs=True)
+    out = captured.allocate_output()
+    call(captured, out)  # an eager call first loads the kernels
+    captured.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        call(captured, out)
+    eager = plan(rows, requests, t["_max_draft"], vocab)
+    expected_out = eager.allocate_output()
+    for case in cases:
+        fresh = device_inputs(case)
+        for name in ["target_logits", "seeds", "positions"]:
+            t[name].copy_(fresh[name])
+        out.tokens.fill_(-777)
+        graph.replay()
+        call(eager, expected_out)
+        torch.cuda.synchronize()
+        assert out.tokens[:requests].tolist() == expected_out.tokens[:requests].tolist()
+        assert out.status[:requests].tolist() == expected_out.status[:requests].tolist()
+    del graph

@@ -305,3 +305,57 @@ def test_results_do_not_depend_on_the_ring_depth(ring, monkeypatch):
         name, subset, digest, expected = entry
         case = golden_io.large_case(name, subset, digest)
         assert_same(run_abi(device_inputs(case), mode=case["mode"]), expected, context=f"{name} ring={ring}")
+
+
+def test_large_batch_is_invariant_to_how_it_is_split():
+    """The reference's large-batch invariance check (tests/invariance/large_gpu.py):
+    1,770 bf16 rows of the full vocabulary (a mix of sampling settings, and
+    verification requests of 1 to 4 drafts) give each request the same
+    outputs whether the batch runs whole or in three uneven parts."""
+    import torch
+    from exactsample_b200.cuda import CudaRequestParams, CudaRngKey, plan, verify
+    g = np.random.default_rng(1770)
+    counts = []
+    while sum(counts) < 1770:
+        counts.append(int(min(g.integers(1, 6), 1770 - sum(counts))))
+    requests = len(counts)
+    cu = np.concatenate([[0], np.cumsum(counts)])
+    rows = int(cu[-1])
+    logits = torch.randn((rows, 151936), dtype=torch.float32, device="cuda") * 2.0
+    peaks = torch.randint(0, 151936, (rows, 64), device="cuda")
+    logits.scatter_add_(1, peaks, torch.rand((rows, 64), device="cuda") * 8 + 8)
+    logits = logits.to(torch.bfloat16)
+    max_draft = max(counts) - 1
+    draft_np = np.full((requests, max_draft), -1, dtype=np.int64)
+    for r, c in enumerate(counts):
+        draft_np[r, :c - 1] = g.integers(0, 151936, c - 1)
+    drafts = torch.as_tensor(draft_np, device="cuda")
+    settings = [(0.6, 20, 0.95, 0.0), (1.0, 0, 1.0, 0.0), (0.8, 0, 0.9, 0.05), (0.0, 0, 1.0, 0.0), (1.2, 50, 1.0, 0.0)]
+    pick = g.integers(0, len(settings), requests)
+    f64 = lambda v: torch.as_tensor(np.asarray(v, np.float64), device="cuda")
+    i64 = lambda v: torch.as_tensor(np.asarray(v, np.int64), device="cuda")
+    params = CudaRequestParams(f64([settings[k][0] for k in pick]), i64([settings[k][1] for k in pick]),
+                               f64([settings[k][2] for k in pick]), f64([settings[k][3] for k in pick]),
+                               i64(np.zeros(requests)))
+    seeds = i64(g.integers(-2**62, 2**62, requests))
+    streams = i64(np.arange(requests))
+    positions = i64(np.concatenate([np.arange(c) + int(g.integers(0, 30000)) for c in counts]))
+
+    def run(r0, r1):
+        a, b = int(cu[r0]), int(cu[r1])
+        work = plan(b - a, r1 - r0, max_draft, 151936)
+        out = work.allocate_output()
+        sub = CudaRequestParams(*(x[r0:r1] for x in (params.temperature, params.top_k, params.top_p, params.min_p,
+                                                     params.draft_kind)))
+        verify(logits[a:b], i64(cu[r0:r1 + 1] - cu[r0]), drafts[r0:r1], params=sub,
+               rng=CudaRngKey(seeds[r0:r1], streams[r0:r1], positions[a:b]), plan=work, out=out)
+        work.synchronize()
+        return out.tokens[:r1 - r0].cpu(), out.accepted_len[:r1 - r0].cpu(), out.status[:r1 - r0].cpu()
+
+    whole = run(0, requests)
+    assert (whole[2] == 0).all()
+    cuts = [0, requests // 7, requests // 2 + 3, requests]
+    parts = [run(a, b) for a, b in zip(cuts, cuts[1:])]
+    for k in range(3):
+        joined = torch.cat([part[k] for part in parts])
+        assert torch.equal(joined, whole[k]), ["tokens", "accepted_len", "status"][k]
