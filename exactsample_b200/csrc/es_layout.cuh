@@ -125,7 +125,8 @@ struct Diagnostics {
 
 // Workspace (bytes): [0] malformed-offsets flag, [4] FP64 recomputation count,
 // [8] RowResult[rows], then one arrival counter per row (used at each
-// request's first row), then Diagnostics, then RowCtx[rows] (16-byte aligned).
+// request's first row), then Diagnostics, then RowCtx[rows] (at the next
+// 16-byte aligned address: the workspace itself need only be 8-byte aligned).
 // Always within the reference's 8 + rows * (32 + 12288) bytes.
 __host__ __device__ inline int32_t* malformed_flag(uint8_t* ws) { return reinterpret_cast<int32_t*>(ws); }
 __host__ __device__ inline uint32_t* fallback_count(uint8_t* ws) { return reinterpret_cast<uint32_t*>(ws + 4); }
@@ -137,12 +138,15 @@ __host__ __device__ inline Diagnostics* diagnostics(uint8_t* ws, int64_t rows) {
   return reinterpret_cast<Diagnostics*>(ws + 8 + rows * (sizeof(RowResult) + 4));
 }
 __host__ __device__ inline RowCtx* row_contexts(uint8_t* ws, int64_t rows) {
-  const uint64_t at = (8 + rows * (sizeof(RowResult) + 4) + sizeof(Diagnostics) + 15) / 16 * 16;
-  return reinterpret_cast<RowCtx*>(ws + at);
+  const uintptr_t at = reinterpret_cast<uintptr_t>(ws) + 8 + rows * (sizeof(RowResult) + 4) + sizeof(Diagnostics);
+  return reinterpret_cast<RowCtx*>((at + 15) & ~uintptr_t(15));
 }
-// Bytes used: at most 8 + 196 * rows + 88 (< the 8 + 12320 * rows provided).
+
+// Bytes used, whatever the workspace's alignment: at most 8 + 116 * rows + 79,
+// far below the 8 + 12320 * rows provided.
 __host__ __device__ inline uint64_t workspace_needed(int64_t rows) {
-  return rows == 0 ? 8 : uint64_t(reinterpret_cast<uintptr_t>(row_contexts(nullptr, rows)) + rows * sizeof(RowCtx));
+  if (rows == 0) return 8;
+  return 8 + uint64_t(rows) * (sizeof(RowResult) + 4) + sizeof(Diagnostics) + 15 + uint64_t(rows) * sizeof(RowCtx);
 }
 
 template <class T> __device__ __forceinline__ T at(const T* p, int64_t stride, int64_t i) { return p[i * stride]; }
@@ -155,7 +159,7 @@ __device__ __forceinline__ void trace_phase(uint8_t* ws, int64_t rows, int row, 
   if (threadIdx.x != 0) return;
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  reinterpret_cast<uint64_t*>(ws + 8 + rows * 256)[(int64_t(row) * 16 + rank) * 16 + k] = t;
+  reinterpret_cast<uint64_t*>(ws + 8 + rows * 1024)[(int64_t(row) * 16 + rank) * 16 + k] = t;
 }
 #define ES_TRACE(ws, rows, row, rank, k) trace_phase(ws, rows, row, rank, k)
 #else

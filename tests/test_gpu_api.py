@@ -167,3 +167,26 @@ def test_capture_is_refused_by_default_and_replays_exactly_with_graphs():
         assert out.tokens[:requests].tolist() == expected_out.tokens[:requests].tolist()
         assert out.status[:requests].tolist() == expected_out.status[:requests].tolist()
     del graph
+
+
+def test_a_workspace_aligned_to_8_bytes_only():
+    """The C ABI asks for an 8-byte aligned workspace (bindings.cpp:106); the
+    per-row records inside it are placed on 16-byte boundaries whatever its
+    alignment, so a workspace at an odd multiple of 8 works the same."""
+    import torch
+    from exactsample_b200 import capi
+    from tests.gpu_helpers import outputs
+    case = C.workload_case("C3a", requests=range(6))
+    t = device_inputs(case)
+    tensors = {k: v for k, v in t.items() if not k.startswith("_")}
+    capi.call(tensors, max_draft=t["_max_draft"])
+    torch.cuda.synchronize()
+    expected = outputs(t)
+    backing = torch.zeros(t["workspace"].numel() + 8, dtype=torch.uint8, device="cuda")
+    tensors["workspace"] = backing[8:]
+    assert tensors["workspace"].data_ptr() % 16 == 8
+    t["tokens"].fill_(-777)
+    capi.call(tensors, max_draft=t["_max_draft"])
+    torch.cuda.synchronize()
+    for got, exp in zip(outputs(t), expected):
+        np.testing.assert_array_equal(got, exp)
