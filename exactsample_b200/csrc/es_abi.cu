@@ -209,7 +209,8 @@ size_t smem_for_dtype(int dtype, int sw, int stages) {
   }
 }
 
-int choose_cluster(int64_t rows, int64_t vocab, int dtype, int* slice_words, size_t* smem, int* stream) {
+int choose_cluster(int64_t rows, int64_t vocab, int dtype, int* slice_words, size_t* smem, int* stream,
+                   int* min_blocks) {
   const int64_t words = (vocab + 31) / 32;
   const size_t row_bytes = size_t(vocab) * element_size(dtype);
   const int resident_min = int(std::max<size_t>(1, (row_bytes + RESIDENT_BYTES - 1) / RESIDENT_BYTES));
@@ -235,26 +236,30 @@ int choose_cluster(int64_t rows, int64_t vocab, int dtype, int* slice_words, siz
     if (forced[0] == '1') streamed = true;
   }
   // The TMA ring: four 16 KB stages while every rank has a place on the GPU
-  // with two per SM; two stages beyond that, so that three ranks fit an SM
-  // (the kernel is then compiled for three blocks per SM; EXACTSAMPLE_RING=2..4
-  // forces the depth).
-  int stages = 0;
-  if (streamed) {
-    stages = rows * c > RESIDENT_SLOTS ? 2 : es::MAX_RING_STAGES;
-    if (const char* forced = std::getenv("EXACTSAMPLE_RING")) {
-      const int n = std::atoi(forced);
-      if (n >= 2 && n <= es::MAX_RING_STAGES) stages = n;
-    }
-  }
+  // with two per SM. Beyond that three ranks share an SM: the kernel is
+  // compiled for three blocks per SM (80 registers) and the ring has two
+  // stages (a third measured no faster). EXACTSAMPLE_RING=2..4 forces the
+  // depth.
+  const bool three = streamed && rows * c > RESIDENT_SLOTS;
   for (;; ++c) {
     if (c > 16) return -1;
     const int sw = int((words + c - 1) / c);
     const int used = int((words + sw - 1) / sw);  // no empty ranks
+    int stages = 0;
+    if (streamed) {
+      stages = es::MAX_RING_STAGES;
+      if (three) stages = 2;
+      if (const char* forced = std::getenv("EXACTSAMPLE_RING")) {
+        const int n = std::atoi(forced);
+        if (n >= 2 && n <= es::MAX_RING_STAGES) stages = n;
+      }
+    }
     const size_t bytes = smem_for_dtype(dtype, sw, stages);
     if (bytes <= MAX_SMEM) {
       *slice_words = sw;
       *smem = bytes;
       *stream = stages;
+      *min_blocks = three ? 3 : 2;
       return used;
     }
   }
@@ -449,7 +454,7 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
   if (rows > 0) {
     // A sharded call finishes about rows / count of the rows on this GPU.
     const int64_t busy = sh != nullptr ? (rows + sh->count - 1) / sh->count : rows;
-    cluster = choose_cluster(busy, vocab, logits.dtype, &p.slice_words, &smem, &p.stream_rows);
+    cluster = choose_cluster(busy, vocab, logits.dtype, &p.slice_words, &smem, &p.stream_rows, &p.min_blocks);
     if (cluster < 0) return fail(ES_ERR_UNSUPPORTED, "vocabulary too large for one 16-block cluster's shared memory");
     const size_t e = element_size(logits.dtype);
     p.vector_load = logits.stride[1] == 1 && reinterpret_cast<uintptr_t>(logits.data) % 16 == 0 &&

@@ -300,7 +300,7 @@ template <int DT> struct RowKernel {
 };
 
 // MIN_BLOCKS: resident CTAs per SM the register allocation must allow (3 for
-// large streamed batches with the 2-stage ring, else 2).
+// large streamed batches, else 2).
 template <int DT, int MIN_BLOCKS>
 __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_constant__ Params p) {
   using K = RowKernel<DT>;
@@ -456,7 +456,7 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_
 // programmatic stream serialization after the preparation kernel.
 template <int DT> cudaError_t launch_rows(const Params& p, int cluster, cudaStream_t stream) {
   const size_t smem = smem_bytes<DT>(p.slice_words, p.stream_rows);
-  auto kernel = p.stream_rows == 2 ? rows_kernel<DT, 3> : rows_kernel<DT, 2>;
+  auto kernel = p.min_blocks == 3 ? rows_kernel<DT, 3> : rows_kernel<DT, 2>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   if (cluster > 8) {

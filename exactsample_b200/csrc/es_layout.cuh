@@ -7,7 +7,8 @@ namespace es {
 
 constexpr int LIST_MAX = 256;   // largest kept set finished as an FP64 list (the plan's list_max caps it)
 static_assert(THREADS >= LIST_MAX, "one thread per list entry");
-constexpr int CAP = 1024;       // candidate buffer of a list row (cluster rank 0's shared memory)
+constexpr int CAP = 512;        // candidate buffer of a list row (cluster rank 0's shared memory)
+static_assert(CAP >= LIST_MAX, "a list's kept tokens fit the candidate buffer");
 constexpr int DIST_BINS = 128;  // distance-below-maximum bins of 0.5 logit, plus one "far" bin
 constexpr int RADIX = 256;      // digits per radix-select level
 constexpr int MAX_RING_STAGES = 4;     // streamed rows: deepest TMA ring
@@ -78,6 +79,7 @@ struct Params {
   int32_t offsets_inline;  // the preparation kernel validates cu_rows itself
   int32_t exact_draws;     // dispatch="reference": every draw scored in FP64, no lists
   int32_t stream_rows;     // 0: rows stay in shared memory; else the depth (2..4) of the TMA ring they stream through
+  int32_t min_blocks;      // blocks per SM the row kernel's registers must allow (2, or 3 for large streamed batches)
   Shards sh;
 };
 
