@@ -73,7 +73,7 @@ template <int DT> struct RowKernel {
   // one per lane: the steps and FP64 formulas of list_finish below, with
   // warp shuffles and ballots in place of block reductions and barriers.
   __device__ static void finish_small(R& r, const RowCtx& c, int n_keep, bool verify, bool full_q, double sq,
-                                      double u_accept, RowResult& res) {
+                                      RowResult& res) {
     constexpr unsigned ALL = 0xffffffffu;
     const int i = lane_id();
     const bool in = i < n_keep;
@@ -101,14 +101,12 @@ template <int DT> struct RowKernel {
       const uint64_t hi = __shfl_up_sync(ALL, uint64_t(prefix >> 64), o);
       if (i >= o) prefix += (u128(hi) << 64) | lo;
     }
-    auto prefix_at = [&](int lane) {
-      const uint64_t lo = __shfl_sync(ALL, uint64_t(prefix), lane);
-      const uint64_t hi = __shfl_sync(ALL, uint64_t(prefix >> 64), lane);
-      return (u128(hi) << 64) | lo;
-    };
-    bool near = false;
-    const double d1 = fx_round(prefix_at(31), uint32_t(n1), &near);
-    r.count_near_tie(near);
+    // Every lane rounds its own prefix (of i + 1 weights) at once: the total
+    // is lane n1 - 1's, the top-p normalizer lane n2 - 1's.
+    bool near_i = false;
+    const double rounded = i < n1 ? fx_round(prefix, uint32_t(i + 1), &near_i) : 0.0;
+    const double d1 = __shfl_sync(ALL, rounded, n1 - 1);
+    r.count_near_tie(__shfl_sync(ALL, near_i, n1 - 1));
     int n2 = n1;
     double denominator = d1;
     if (r.top_p < 1) {
@@ -121,8 +119,8 @@ template <int DT> struct RowKernel {
         const unsigned hits = __ballot_sync(ALL, reach);
         n2 = hits ? __ffs(hits) : n1;
       }
-      denominator = fx_round(prefix_at(n2 - 1), uint32_t(n2), &near);
-      r.count_near_tie(near);
+      denominator = __shfl_sync(ALL, rounded, n2 - 1);
+      r.count_near_tie(__shfl_sync(ALL, near_i, n2 - 1));
     }
     const double prob = i < n2 ? w / denominator : 0.0;
     ES_TRACE(r.p.workspace, r.p.rows, r.row, r.rank, 12);
@@ -143,7 +141,7 @@ template <int DT> struct RowKernel {
     const double p_draft = __shfl_sync(ALL, prob, at_draft ? __ffs(at_draft) - 1 : 0);
     const double px = at_draft ? p_draft : 0.0;
     const double qx = q_of_draft(r, c, full_q, sq);
-    res.accept = u_accept < fmin(1.0, px / qx);
+    res.accept = uniform64(r.addr.word(1, 0)) < fmin(1.0, px / qx);
     if (res.accept) return;
     if (!full_q) {
       res.residual = draw_list(2, c.draft_id);
@@ -163,12 +161,12 @@ template <int DT> struct RowKernel {
   // Rank 0 finishes a list row: the m gathered candidates hold the kept
   // n_keep tokens first once sorted. Oracle formulas throughout (FP64).
   __device__ static void list_finish(R& r, const RowCtx& c, int m, int n_keep, bool verify, bool full_q, double sq,
-                                     double u_accept, RowResult& res) {
+                                     RowResult& res) {
     auto& s = r.s;
     r.sort_candidates(m);
     ES_TRACE(r.p.workspace, r.p.rows, r.row, r.rank, 10);
     if (n_keep <= 32) {
-      if (warp_id() == 0) finish_small(r, c, n_keep, verify, full_q, sq, u_accept, res);
+      if (warp_id() == 0) finish_small(r, c, n_keep, verify, full_q, sq, res);
       return;
     }
     const int i = threadIdx.x;
@@ -228,7 +226,7 @@ template <int DT> struct RowKernel {
                                    s.red.ints);
     const double px = at_draft == INT_MAX ? 0.0 : s.lp[at_draft];
     const double qx = q_of_draft(r, c, full_q, sq);
-    res.accept = u_accept < fmin(1.0, px / qx);
+    res.accept = uniform64(r.addr.word(1, 0)) < fmin(1.0, px / qx);
     if (res.accept) return;
     if (!full_q) {
       res.residual = draw_list(2, c.draft_id);
@@ -253,7 +251,6 @@ template <int DT> struct RowKernel {
     const int64_t k = c.top_k;
     const int n_keep = (k > 0 && k < valid) ? int(k) : valid;
     const int list_max = p.exact_draws ? 0 : min(p.list_max, LIST_MAX);
-    const double u_accept = uniform64(r.addr.word(1, 0));
     if (n_keep <= list_max) {
       int m;
       if (n_keep < valid) {
@@ -266,7 +263,7 @@ template <int DT> struct RowKernel {
       } else {
         m = r.gather_all([](W, int) { return true; });
       }
-      if (r.rank == 0) list_finish(r, c, m, n_keep, verify, full_q, sq, u_accept, res);
+      if (r.rank == 0) list_finish(r, c, m, n_keep, verify, full_q, sq, res);
       return true;
     }
     Cut<Key> cut_k{0, 0, 0}, cut_p{0, 0, 0};
@@ -292,7 +289,7 @@ template <int DT> struct RowKernel {
         if (w >= r.min_p && w > 0) px = w / sp;
       }
     }
-    res.accept = u_accept < fmin(1.0, px / q_of_draft(r, c, full_q, sq));
+    res.accept = uniform64(r.addr.word(1, 0)) < fmin(1.0, px / q_of_draft(r, c, full_q, sq));
     if (res.accept) return false;
     res.residual = full_q ? r.draw_residual_q(kept, sp, sq) : r.draw(2, x, kept, p.exact_draws != 0);
     return false;
