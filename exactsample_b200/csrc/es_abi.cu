@@ -24,6 +24,7 @@ __global__ void __launch_bounds__(1024) check_offsets(const __grid_constant__ Pa
 // One thread per request: outputs reset to the failed state (tokens -1,
 // accepted 0), metadata status, path, and the request's arrival counter.
 __global__ void __launch_bounds__(128) prepare(const __grid_constant__ Params p) {
+  if (blockIdx.x == 0) ES_TRACE(p.workspace, p.rows, 0, 15, 0);  // development builds: when preparation starts
   allow_dependent_grid();  // the row kernel may launch now and start loading logits
   // A vocabulary-sharded call: the stream's earlier work (this GPU's shard)
   // is done, so tell the peers.
@@ -83,6 +84,7 @@ __global__ void __launch_bounds__(128) prepare(const __grid_constant__ Params p)
     }
     out[row] = c;
   }
+  if (blockIdx.x == 0) ES_TRACE(p.workspace, p.rows, 0, 15, 1);  // development builds: block 0 done
 }
 
 // Vocabulary-sharded calls: a GPU's "shard written" and "outputs done" flags.

@@ -364,9 +364,8 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_
     for (int w = threadIdx.x; w < (n + 31) / 32; w += THREADS)
       mask_s[w] = uint32_t(p.mask[int64_t(r.row) * p.m_s0 + int64_t(r.lo / 32 + w) * p.m_s1]);
 
-  // 2. The preparation kernel's statuses and counters, then the copy.
-  wait_for_prerequisite_grid();
-  ES_TRACE(p.workspace, p.rows, r.row, r.rank, 1);
+  // 2. The copy (resident rows). The preparation kernel's outputs are not
+  //    needed before the statistics, so it runs alongside them.
   for (uint32_t spins = 0; !mbar_try_wait(&s.bar, 0);)
     if (++spins >= WAIT_LIMIT) {
       lost = true;
@@ -376,8 +375,14 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_
   ES_TRACE(p.workspace, p.rows, r.row, r.rank, 2);
   if (lost && threadIdx.x == 0) atomicAdd(&diagnostics(p.workspace, p.rows)->wait_timeouts, 1u);
 
-  // 3. The row's request and parameters (the same on every rank), gathered
-  //    by the preparation kernel.
+  // 3. Validation and the row maximum.
+  r.stats_pass(lost);
+  ES_TRACE(p.workspace, p.rows, r.row, r.rank, 3);
+
+  // 4. The preparation kernel's statuses and counters; the row's request and
+  //    parameters (the same on every rank), gathered by it.
+  wait_for_prerequisite_grid();
+  ES_TRACE(p.workspace, p.rows, r.row, r.rank, 1);
   if (threadIdx.x == 0) {
     if (*malformed_flag(p.workspace) != 0) {
       s.ctx.skip = 1;
@@ -386,11 +391,8 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_
     }
   }
   __syncthreads();
-  if (s.ctx.skip) {  // the same decision on every rank; no rank reads another's memory
-    if (stream && p.vector_load && threadIdx.x == 0)  // let the ring copies land before leaving
-      for (int c = 0; c < min(p.stream_rows, r.ring_chunks()); ++c)
-        for (uint32_t spins = 0; !mbar_try_wait(&s.ring_bar[c], 0) && spins < (1u << 22); ++spins) {
-        }
+  if (s.ctx.skip) {  // the same decision on every rank; every copy has landed
+    r.cluster.sync();  // no rank leaves while a peer may still read its statistics slot
     return;
   }
   const RowCtx c = s.ctx;
@@ -400,10 +402,7 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_
   r.top_p = c.top_p;
   r.min_p = c.min_p;
   r.addr = Address{c.stream, c.position, uint32_t(c.seed), uint32_t(c.seed >> 32)};
-
-  // 4. Validation and the row maximum.
-  r.stats_pass(full_q, lost);
-  ES_TRACE(p.workspace, p.rows, r.row, r.rank, 3);
+  if (full_q) r.q_stats_pass();  // the same on every rank
   RowResult res{ES_OK, ES_OK, 0, -1, -1, {0, 0, 0}};
   res.target_status = r.all.bad ? ES_INVALID_INPUT : r.all.valid == 0 ? ES_NO_VALID_TOKEN : ES_OK;
   res.status = res.target_status;

@@ -496,7 +496,7 @@ template <int DT> struct Row {
   // The statistics pass over the whole slice: from shared memory (resident),
   // through the TMA ring (streamed, 16-byte aligned rows), or from global
   // memory; then the cluster merge. Returns false if a copy never arrived.
-  __device__ bool stats_pass(bool full_q, bool timed_out) {
+  __device__ bool stats_pass(bool timed_out) {
     Acc a{W(-INFINITY), 0, 0};
     bool lost = timed_out;
     if (resident) {
@@ -522,18 +522,9 @@ template <int DT> struct Row {
     } else {
       stats_groups(0, groups, [&](int g, W v[4]) { values(g, v); }, a);
     }
-    W qmax = W(-INFINITY);
-    int qvalid = 0, qbad = 0;
-    if (full_q)
-      for (int t = lo + int(threadIdx.x); t < hi; t += THREADS) {
-        const W y = q_value(t);
-        qbad |= isnan(y) | (y == W(INFINITY));
-        qvalid += y > W(-INFINITY);
-        qmax = y > qmax ? y : qmax;
-      }
     lost = __syncthreads_or(lost);
     if (lost) a.bad = 1;  // a slice copy never arrived: the row is not trusted
-    const Stats<W> merged = block_stats(Stats<W>{a.best, qmax, a.valid, a.bad, qvalid, qbad});
+    const Stats<W> merged = block_stats(Stats<W>{a.best, W(-INFINITY), a.valid, a.bad, 0, 0});
     if (threadIdx.x == 0) s.stats[parity()] = merged;
     ES_TRACE(p.workspace, p.rows, row, rank, 8);
     exchange();
@@ -545,6 +536,30 @@ template <int DT> struct Row {
     maxv = all.vmax;
     __syncthreads();
     return !lost;
+  }
+
+  // The proposal row's checks (NaN / +inf, valid count) and maximum, for a
+  // full-q draft row, merged over the cluster into all.qmax / qvalid / qbad.
+  __device__ void q_stats_pass() {
+    W qmax = W(-INFINITY);
+    int qvalid = 0, qbad = 0;
+    for (int t = lo + int(threadIdx.x); t < hi; t += THREADS) {
+      const W y = q_value(t);
+      qbad |= isnan(y) | (y == W(INFINITY));
+      qvalid += y > W(-INFINITY);
+      qmax = y > qmax ? y : qmax;
+    }
+    const Stats<W> merged = block_stats(Stats<W>{W(-INFINITY), qmax, 0, 0, qvalid, qbad});
+    if (threadIdx.x == 0) s.stats[parity()] = merged;
+    exchange();
+    if (int(threadIdx.x) < ranks) s.peers.stats[threadIdx.x] = *peer(&s.stats[parity() ^ 1], threadIdx.x);
+    __syncthreads();
+    Stats<W> q = s.peers.stats[0];
+    for (int r = 1; r < ranks; ++r) q = merge_stats(q, s.peers.stats[r]);
+    all.qmax = q.qmax;
+    all.qvalid = q.qvalid;
+    all.qbad = q.qbad;
+    __syncthreads();
   }
 
   // ---- cluster-wide reductions ----
