@@ -72,8 +72,9 @@ template <int DT> struct RowKernel {
   // Warp 0 of rank 0 finishes a sorted list of n_keep <= 32 kept tokens,
   // one per lane: the steps and FP64 formulas of list_finish below, with
   // warp shuffles and ballots in place of block reductions and barriers.
-  __device__ static void finish_small(R& r, const RowCtx& c, int n_keep, bool verify, bool full_q, double sq,
-                                      RowResult& res) {
+  // Returns false, with nothing written, where list_finish does.
+  __device__ static bool finish_small(R& r, const RowCtx& c, int n_keep, bool verify, bool full_q, double sq,
+                                      RowResult& res, Interval open) {
     constexpr unsigned ALL = 0xffffffffu;
     const int i = lane_id();
     const bool in = i < n_keep;
@@ -110,14 +111,23 @@ template <int DT> struct RowKernel {
     int n2 = n1;
     double denominator = d1;
     if (r.top_p < 1) {
-      const double target = r.top_p * d1;
-      if (target <= 1.0) {
-        n2 = 1;  // the first token's weight is exactly 1
-      } else {
+      // The length of the shortest prefix whose rounded sum reaches t (0 if
+      // none in the list); the first token's weight is exactly 1.
+      auto first_reach = [&](double t) {
+        if (t <= 1.0) return 1;
         bool nr = false;
-        const bool reach = i < n1 && fx_reaches(prefix, uint32_t(i + 1), target, &nr);
-        const unsigned hits = __ballot_sync(ALL, reach);
-        n2 = hits ? __ffs(hits) : n1;
+        const unsigned hits = __ballot_sync(ALL, i < n1 && fx_reaches(prefix, uint32_t(i + 1), t, &nr));
+        return hits ? __ffs(hits) : 0;
+      };
+      if (open.hi > 0 && n1 == n_keep) {
+        // The kept set may run past the list: the boundary must be the same
+        // for every target within the bounds.
+        const int a = first_reach(open.lo), b = first_reach(open.hi);
+        if (b == 0 || a != b) return false;
+        n2 = b;
+      } else {
+        const int f = first_reach(r.top_p * d1);
+        n2 = f ? f : n1;
       }
       denominator = __shfl_sync(ALL, rounded, n2 - 1);
       r.count_near_tie(__shfl_sync(ALL, near_i, n2 - 1));
@@ -135,17 +145,17 @@ template <int DT> struct RowKernel {
     if (!verify) {
       res.sample = draw_list(0, -1);
       ES_TRACE(r.p.workspace, r.p.rows, r.row, r.rank, 15);
-      return;
+      return true;
     }
     const unsigned at_draft = __ballot_sync(ALL, i < n2 && id == c.draft_id);
     const double p_draft = __shfl_sync(ALL, prob, at_draft ? __ffs(at_draft) - 1 : 0);
     const double px = at_draft ? p_draft : 0.0;
     const double qx = q_of_draft(r, c, full_q, sq);
     res.accept = uniform64(r.addr.word(1, 0)) < fmin(1.0, px / qx);
-    if (res.accept) return;
+    if (res.accept) return true;
     if (!full_q) {
       res.residual = draw_list(2, c.draft_id);
-      return;
+      return true;
     }
     Best b = no_best();
     if (i < n2 && prob > 0) {
@@ -156,18 +166,33 @@ template <int DT> struct RowKernel {
     }
     b = warp_all(b, [](Best a, Best c2) { return best_of(a, c2); });
     res.residual = b.id == INT_MAX ? -1 : b.id;
+    return true;
   }
 
   // Rank 0 finishes a list row: the m gathered candidates hold the kept
   // n_keep tokens first once sorted. Oracle formulas throughout (FP64).
-  __device__ static void list_finish(R& r, const RowCtx& c, int m, int n_keep, bool verify, bool full_q, double sq,
-                                     RowResult& res) {
+  //
+  // With open.hi > 0, the list holds only the n_keep largest tokens of a kept
+  // set that may run past it (top-p without top-k), and `open` bounds the oracle's
+  // top-p target, top_p * fsum(kept set). The nucleus is settled when the
+  // shortest prefix reaching the target is the same for every target within
+  // the bounds, or when min-p ends the kept set inside the list (its sum is
+  // then exact); otherwise the call returns false with nothing written.
+  // Block-uniform result.
+  __device__ static bool list_finish(R& r, const RowCtx& c, int m, int n_keep, bool verify, bool full_q, double sq,
+                                     RowResult& res, Interval open) {
     auto& s = r.s;
     r.sort_candidates(m);
     ES_TRACE(r.p.workspace, r.p.rows, r.row, r.rank, 10);
     if (n_keep <= 32) {
-      if (warp_id() == 0) finish_small(r, c, n_keep, verify, full_q, sq, res);
-      return;
+      if (threadIdx.x == 0) s.ival[3] = 0;
+      __syncthreads();
+      if (warp_id() == 0) {
+        const bool settled = finish_small(r, c, n_keep, verify, full_q, sq, res, open);
+        if (lane_id() == 0) s.ival[3] = settled;
+      }
+      __syncthreads();
+      return s.ival[3] != 0;
     }
     const int i = threadIdx.x;
     const bool in = i < n_keep;
@@ -191,14 +216,22 @@ template <int DT> struct RowKernel {
     int n2 = n1;
     double denominator = d1;
     if (r.top_p < 1) {
-      const double target = r.top_p * d1;
-      if (target <= 1.0) {
-        n2 = 1;  // the first token's weight is exactly 1
-      } else {
+      // The length of the shortest prefix whose rounded sum reaches t (0 if
+      // none in the list); the first token's weight is exactly 1.
+      auto first_reach = [&](double t) {
+        if (t <= 1.0) return 1;
         bool nr = false;
-        const bool reach = i < n1 && fx_reaches(prefix, uint32_t(i + 1), target, &nr);
+        const bool reach = i < n1 && fx_reaches(prefix, uint32_t(i + 1), t, &nr);
         const int first = block_all(reach ? i : INT_MAX, [](int a, int b) { return a < b ? a : b; }, s.red.ints);
-        n2 = first == INT_MAX ? n1 : first + 1;
+        return first == INT_MAX ? 0 : first + 1;
+      };
+      if (open.hi > 0 && n1 == n_keep) {
+        const int a = first_reach(open.lo), b = first_reach(open.hi);
+        if (b == 0 || a != b) return false;
+        n2 = b;
+      } else {
+        const int f = first_reach(r.top_p * d1);
+        n2 = f ? f : n1;
       }
       if (i == n2 - 1) s.fxval = prefix;
       __syncthreads();
@@ -220,17 +253,17 @@ template <int DT> struct RowKernel {
     if (!verify) {
       res.sample = draw_list(0, -1);
       ES_TRACE(r.p.workspace, r.p.rows, r.row, r.rank, 12);
-      return;
+      return true;
     }
     const int at_draft = block_all(i < n2 && id == c.draft_id ? i : INT_MAX, [](int a, int b) { return a < b ? a : b; },
                                    s.red.ints);
     const double px = at_draft == INT_MAX ? 0.0 : s.lp[at_draft];
     const double qx = q_of_draft(r, c, full_q, sq);
     res.accept = uniform64(r.addr.word(1, 0)) < fmin(1.0, px / qx);
-    if (res.accept) return;
+    if (res.accept) return true;
     if (!full_q) {
       res.residual = draw_list(2, c.draft_id);
-      return;
+      return true;
     }
     Best b = no_best();
     if (i < n2 && prob > 0) {
@@ -241,6 +274,7 @@ template <int DT> struct RowKernel {
     }
     b = block_all(b, [](Best a, Best c2) { return best_of(a, c2); }, s.red.bests);
     res.residual = b.id == INT_MAX ? -1 : b.id;
+    return true;
   }
 
   // Returns true when rank 0 finishes the row alone (a list row): the other
@@ -251,47 +285,89 @@ template <int DT> struct RowKernel {
     const int64_t k = c.top_k;
     const int n_keep = (k > 0 && k < valid) ? int(k) : valid;
     const int list_max = p.exact_draws ? 0 : min(p.list_max, LIST_MAX);
-    if (n_keep <= list_max) {
-      int m;
-      if (n_keep < valid) {
-        m = r.gather_near(n_keep);
-        ES_TRACE(p.workspace, p.rows, r.row, r.rank, 5);
-        if (m < 0) {
-          const Cut<Key> cut = r.select_nth(n_keep, [](Key, int, W) { return true; });
-          m = r.gather_all([&](W v, int t) { return cut.keeps(order_key(v), t); });
+    // A list row: the kept set is at most list_max tokens. Otherwise top-p
+    // without top-k: on real logits the nucleus is a handful of the largest
+    // tokens, so lists of the largest 32, then list_max, tokens are tried
+    // against bounds on the kept set's total, and the exact full-row
+    // selection below decides when neither list settles the boundary.
+    const bool list_row = n_keep <= list_max;
+    const bool top_p_list = !list_row && n_keep == valid && r.top_p < 1 && list_max > 0;
+    Interval target{0, 0};
+    if (top_p_list) {
+      const Interval total = r.approx_mass([](Key, int) { return true; }, false);
+      target = Interval{r.top_p * total.lo, r.top_p * total.hi};  // rounding is monotone
+    }
+    int tried = 0;
+    for (int attempt = 0; attempt < (list_row ? 1 : top_p_list ? 2 : 0); ++attempt) {
+      int m, len = n_keep;
+      Interval open{0, 0};
+      if (list_row) {
+        if (n_keep < valid) {
+          m = r.gather_near(n_keep);
+          ES_TRACE(p.workspace, p.rows, r.row, r.rank, 5);
+          if (m < 0) {
+            const Cut<Key> cut = r.select_nth(n_keep, [](Key, int, W) { return true; });
+            m = r.gather_all([&](W v, int t) { return cut.keeps(order_key(v), t); });
+          }
+        } else {
+          m = r.gather_all([](W, int) { return true; });
         }
       } else {
-        m = r.gather_all([](W, int) { return true; });
+        const int want = min(attempt == 0 ? 32 : list_max, valid);
+        if (want <= tried) break;
+        m = r.gather_near(want);
+        if (m < 0) break;  // the same on every rank
+        len = min(m, list_max);
+        if (len < valid) open = target;
       }
-      if (r.rank == 0) list_finish(r, c, m, n_keep, verify, full_q, sq, res);
-      return true;
+      bool settled = false;
+      if (r.rank == 0) settled = list_finish(r, c, m, len, verify, full_q, sq, res, open);
+      if (list_row) return true;
+      if (r.broadcast_verdict(settled)) return true;
+      tried = len;
     }
     Cut<Key> cut_k{0, 0, 0}, cut_p{0, 0, 0};
     if (k > 0 && k < valid) cut_k = r.select_nth(int(k), [](Key, int, W) { return true; });
+    ES_TRACE(p.workspace, p.rows, r.row, r.rank, 4);
     double sp = 0;
     bool sp_known = false;
     if (r.top_p < 1) {
       cut_p = r.top_p_cut(cut_k, &sp);
       sp_known = true;
     }
+    ES_TRACE(p.workspace, p.rows, r.row, r.rank, 5);
     auto kept = [cut_k, cut_p](Key key, int t) { return cut_k.keeps(key, t) && cut_p.keeps(key, t); };
+    const bool cuts = cut_k.on || cut_p.on;
     if (!verify) {
-      res.sample = r.draw(0, -1, kept, p.exact_draws != 0);
+      res.sample = r.draw(0, -1, kept, cuts, p.exact_draws != 0);
+      ES_TRACE(p.workspace, p.rows, r.row, r.rank, 12);
       return false;
     }
-    if (!sp_known) sp = r.exact_mass(kept);
     const int x = c.draft_id;
-    double px = 0;
+    double wx = 0;  // the draft token's weight, if kept
     if (r.valid_global(x)) {
       const W v = r.value_global(x);
       if (kept(order_key(v), x)) {
         const double w = exp(r.x64(v));
-        if (w >= r.min_p && w > 0) px = w / sp;
+        if (w >= r.min_p && w > 0) wx = w;
       }
     }
-    res.accept = uniform64(r.addr.word(1, 0)) < fmin(1.0, px / q_of_draft(r, c, full_q, sq));
+    const double qx = q_of_draft(r, c, full_q, sq);
+    const double u = uniform64(r.addr.word(1, 0));
+    // The oracle's test u < min(1, (wx / sp) / qx) falls as sp grows (every
+    // step rounds monotonically), so bounds on sp usually settle it without
+    // the exact sum, which one-hot residual draws do not need either.
+    int accept = wx == 0 ? 0 : -1;
+    if (accept < 0 && !sp_known && !p.exact_draws) {
+      const Interval m = r.approx_mass(kept, cuts);
+      if (u < fmin(1.0, (wx / m.hi) / qx)) accept = 1;
+      else if (m.lo > 0 && !(u < fmin(1.0, (wx / m.lo) / qx))) accept = 0;
+    }
+    if (!sp_known && (accept < 0 || (accept == 0 && full_q))) sp = r.exact_mass(kept);
+    if (accept < 0) accept = u < fmin(1.0, (wx / sp) / qx);
+    res.accept = accept != 0;
     if (res.accept) return false;
-    res.residual = full_q ? r.draw_residual_q(kept, sp, sq) : r.draw(2, x, kept, p.exact_draws != 0);
+    res.residual = full_q ? r.draw_residual_q(kept, sp, sq) : r.draw(2, x, kept, cuts, p.exact_draws != 0);
     return false;
   }
 };
@@ -347,7 +423,7 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_
     if (threadIdx.x == 0) {
       mbar_arrive_expect_tx(&s.bar, 0);
       if (p.vector_load)
-        for (int c = 0; c < min(p.stream_rows, r.ring_chunks()); ++c) r.ring_issue(c);
+        for (int c = 0; c < min(p.stream_rows, r.ring_chunks()); ++c) r.ring_issue(c, c);
     }
   } else if (p.vector_load) {
     const uint32_t bytes = uint32_t(n) * uint32_t(sizeof(T)), bulk = bytes & ~15u;
@@ -438,6 +514,10 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_
   if (!solo) r.cluster.sync();  // no rank reads another's shared memory after this point
   ES_TRACE(p.workspace, p.rows, r.row, r.rank, 7);
   if (r.rank == 0 && threadIdx.x == 0) {
+    if (s.timeout != 0) {  // a copy of a later pass never arrived on some rank: the row is not trusted
+      res.target_status = ES_INVALID_INPUT;
+      res.status = ES_INVALID_INPUT;
+    }
     row_results(p.workspace)[r.row] = res;
     __threadfence();
     const uint32_t done = atomicAdd(&arrivals(p.workspace, p.rows)[c.begin], 1u) + 1;

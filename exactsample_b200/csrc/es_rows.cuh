@@ -96,6 +96,11 @@ constexpr float SCORE_ERR = 1.5e-6f;
 // Tokens are pruned only this far below the best lower bound so far, so a
 // pruned bound rarely blocks the certificate of a different winner.
 constexpr float PRUNE_MARGIN = 1e-3f;
+// NOISE_MAX + SCORE_ERR (1 + NOISE_MAX): the noise part of the largest score
+// bound a token with x <= 0 can have.
+constexpr float LIVE_OFFSET = NOISE_MAX + SCORE_ERR * (1.f + NOISE_MAX);
+// A float at least ln 2.
+constexpr float LN2_UP = 0.69314725f;
 // Distance windows (logits below the maximum) tried for list candidates.
 constexpr int WINDOWS = 8;
 __device__ __forceinline__ float window_width(int i) { return 0.25f * float(1 << i); }  // 0.25 .. 32
@@ -111,6 +116,24 @@ template <class W> struct Stats {
   W vmax, qmax;  // largest valid target value; largest proposal value (full q)
   int32_t valid, bad, qvalid, qbad;
 };
+
+// A rank's share of an approximate kept-set mass (approx_mass): FP32 weights
+// summed in FP64, split by whether min-p certainly keeps the token.
+struct MassPart {
+  double kept;   // weights of tokens min-p certainly keeps
+  double unsure; // weights of tokens too close to the min-p threshold to tell
+  double err;    // bound on the error of the two sums
+  uint32_t n;    // tokens in either
+};
+// Bounds on a sum: lo <= exact <= hi.
+struct Interval {
+  double lo, hi;
+};
+// |__expf(x32) - exp(x)| <= MASS_ERR (1 + |x|) __expf(x32): X_ERR |x| from
+// x32, and __expf's documented bound of (2 + 1.173 |x|) ulp (CUDA C++
+// Programming Guide, intrinsic functions), with a factor of about three to
+// spare.
+constexpr double MASS_ERR = 1.0e-6;
 // Candidate tiles (32 tokens) a rank scans for list candidates before it
 // falls back to a full pass.
 constexpr int TILE_CAP = 256;
@@ -128,6 +151,7 @@ template <class W> struct Smem {
   uint32_t fxn[2];
   Pick pick[2];
   Best best[2];
+  MassPart mass_part[2];
   int32_t slot[2];
   // Block scratch.
   union {
@@ -138,6 +162,7 @@ template <class W> struct Smem {
     uint32_t uints[WARPS];
     int32_t win[WARPS][WINDOWS];
     Stats<W> stats[WARPS];
+    MassPart masses[WARPS];
   } red;
   // Peers' published slots, copied here by a few threads after an exchange.
   union {
@@ -145,10 +170,12 @@ template <class W> struct Smem {
     Pick picks[16];
     Best bests[16];
     u128 fx[16];
+    MassPart masses[16];
     int32_t ints[16 * WINDOWS + 16];
   } peers;
   uint32_t peer_n[16];
   int32_t pushed[16];  // per-rank counts each rank writes into every rank's copy
+  int32_t verdict;     // rank 0's decision on a top-p list, written into every rank's copy
   int32_t tiles[TILE_CAP];
   int32_t n_tiles;
   int32_t ival[4];
@@ -207,9 +234,11 @@ template <int DT> struct Row {
   T* slice;          // this rank's logits (resident rows) or the TMA ring (streamed rows)
   const T* tbase;    // the row in global memory (not sharded)
   bool resident, vec, sharded;
+  bool dense;  // after the statistics: no mask and every token of the row valid
   cg::cluster_group cluster;
   int rank, ranks, row, lo, hi, groups;
   int xc;  // exchanges so far (the same on every rank)
+  int ring_seq;  // streamed rows: chunks the TMA ring has carried so far (fixes each stage's phase)
   int argmax_;  // the greedy token once argmax_id() has found it, else -1
 
   // Row-level values, identical on every rank after the statistics merge.
@@ -229,11 +258,13 @@ template <int DT> struct Row {
     hi = min(p.vocab, lo + p.slice_words * 32);
     groups = (hi - lo + 3) / 4;
     xc = 0;
+    ring_seq = 0;
     argmax_ = -1;
     has_mask = p.mask != nullptr;
     resident = !p.stream_rows;
     vec = p.vector_load != 0;
     sharded = p.sh.count > 1;
+    dense = false;
     tbase = static_cast<const T*>(p.target) + int64_t(row) * p.t_s0;
   }
 
@@ -484,10 +515,11 @@ template <int DT> struct Row {
   // Bytes of the slice the TMA ring carries (whole 16-byte units), in chunks.
   __device__ __forceinline__ uint32_t ring_bytes() const { return (uint32_t(hi - lo) * uint32_t(sizeof(T))) & ~15u; }
   __device__ __forceinline__ int ring_chunks() const { return int((ring_bytes() + RING_CHUNK - 1) / RING_CHUNK); }
-  // Thread 0 starts the TMA copy of chunk c into its ring stage.
-  __device__ __forceinline__ void ring_issue(int c) {
+  // Thread 0 starts the TMA copy of chunk c into the ring stage of the
+  // ring's seq-th use.
+  __device__ __forceinline__ void ring_issue(int c, int seq) {
     const uint32_t off = uint32_t(c) * RING_CHUNK, len = min(RING_CHUNK, ring_bytes() - off);
-    const int stage = c % p.stream_rows;
+    const int stage = seq % p.stream_rows;
     uint64_t* bar = &s.ring_bar[stage];
     mbar_arrive_expect_tx(bar, len);
     bulk_columns(reinterpret_cast<uint8_t*>(slice) + stage * RING_CHUNK, lo + int(off / sizeof(T)),
@@ -516,8 +548,9 @@ template <int DT> struct Row {
         stats_groups(c * GPC, min((c + 1) * GPC, ring_groups),
                      [&](int g, W v[4]) { load4(stage + 4 * g, v); }, a);
         __syncthreads();  // every thread is done with this stage
-        if (threadIdx.x == 0 && c + stages < chunks) ring_issue(c + stages);
+        if (threadIdx.x == 0 && c + stages < chunks) ring_issue(c + stages, c + stages);
       }
+      ring_seq = chunks;
       stats_groups(ring_groups, groups, [&](int g, W v[4]) { values(g, v); }, a);  // the last partial tile
     } else {
       stats_groups(0, groups, [&](int g, W v[4]) { values(g, v); }, a);
@@ -534,8 +567,66 @@ template <int DT> struct Row {
     all = s.peers.stats[0];
     for (int r = 1; r < ranks; ++r) all = merge_stats(all, s.peers.stats[r]);
     maxv = all.vmax;
+    dense = !has_mask && all.valid == p.vocab;
     __syncthreads();
     return !lost;
+  }
+
+  // A later pass over the slice: f(g, v, bits) for every group g, with v its
+  // four values and bits its valid tokens (allowed, inside the slice, above
+  // -inf). All lanes of a warp call f together (past the slice with bits 0),
+  // so f may use warp collectives. Resident rows read shared memory;
+  // streamed rows go through the TMA ring again, which keeps 16 KB stages in
+  // flight where plain loads would keep a few hundred bytes per warp. A copy
+  // that never arrives (a bounded wait) marks the row on rank 0.
+  template <class F> __device__ void slice_pass(F f) {
+    constexpr int GPC = int(RING_CHUNK / (4 * sizeof(T)));  // groups per chunk
+    const bool ring = !resident && vec;
+    const int ring_groups = ring ? int(ring_bytes() / (4 * sizeof(T))) & ~7 : 0;
+    const int chunks = ring ? ring_chunks() : 0, stages = p.stream_rows;
+    if (threadIdx.x == 0)
+      for (int c = 0; c < min(stages, chunks); ++c) ring_issue(c, ring_seq + c);
+    bool lost = false;
+    // Segments: the ring's chunks, then the rest of the slice (all of it for
+    // resident rows) from shared or global memory. One call site for f.
+    for (int c = 0; c <= chunks; ++c) {
+      const int seq = ring_seq + c;
+      int g0 = ring_groups, g1 = groups;
+      const T* src = resident ? slice : nullptr;
+      if (c < chunks) {
+        for (uint32_t spins = 0; !lost && !mbar_try_wait(&s.ring_bar[seq % stages], uint32_t(seq / stages) & 1u);)
+          if (++spins >= (1u << 22)) lost = true;
+        src = slice + (seq % stages) * (RING_CHUNK / sizeof(T)) - int64_t(c) * GPC * 4;
+        g0 = c * GPC;
+        g1 = min(g0 + GPC, ring_groups);
+      }
+      auto load = [&](int g, W* v) {
+        if (src == nullptr) return group(g, v);
+        load4(src + 4 * g, v);
+        unsigned bits = group_bits(g);
+        if (!dense)
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (!(v[j] > W(-INFINITY))) bits &= ~(1u << j);
+        return bits;
+      };
+      for (int base = g0 + warp_id() * 32; base < g1; base += THREADS) {
+        const int g = base + lane_id();
+        W v[4] = {W(-INFINITY), W(-INFINITY), W(-INFINITY), W(-INFINITY)};
+        unsigned bits = 0;
+        if (g < g1) bits = load(g, v);
+        f(g, v, bits);
+      }
+      if (c < chunks) {
+        lost = __syncthreads_or(lost);  // every thread is done with this stage
+        if (threadIdx.x == 0 && c + stages < chunks) ring_issue(c + stages, seq + stages);
+      }
+    }
+    ring_seq += chunks;
+    if (lost && threadIdx.x == 0) {
+      atomicAdd(&diagnostics(p.workspace, p.rows)->wait_timeouts, 1u);
+      atomicOr(peer(&s.timeout, 0), 1);
+    }
   }
 
   // The proposal row's checks (NaN / +inf, valid count) and maximum, for a
@@ -623,11 +714,7 @@ template <int DT> struct Row {
       uint32_t* h = s.hist[parity()];
       for (int i = threadIdx.x; i < RADIX; i += THREADS) h[i] = 0;
       __syncthreads();
-      for (int base = warp_id() * 32; base < groups; base += THREADS) {
-        const int g = base + lane_id();
-        W v[4];
-        unsigned bits = 0;
-        if (g < groups) bits = group(g, v);
+      slice_pass([&](int g, const W* v, unsigned bits) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           int d = -1;
@@ -637,7 +724,7 @@ template <int DT> struct Row {
           }
           warp_bucket_add(nullptr, h, d, 0);
         }
-      }
+      });
       exchange();
       // Thread i owns digit 255 - i: merged counts, scanned from the top.
       if (threadIdx.x == 0) { s.ival[0] = 0; s.ival[1] = 0; }
@@ -955,9 +1042,7 @@ template <int DT> struct Row {
   template <class Kept> __device__ double exact_mass(Kept kept) {
     u128 acc = 0;
     uint32_t n = 0;
-    for (int g = threadIdx.x; g < groups; g += THREADS) {
-      W v[4];
-      const unsigned bits = group(g, v);
+    slice_pass([&](int g, const W* v, unsigned bits) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         if (!((bits >> j) & 1u) || !kept(order_key(v[j]), lo + 4 * g + j)) continue;
@@ -966,7 +1051,7 @@ template <int DT> struct Row {
         acc += fx_of(w);
         ++n;
       }
-    }
+    });
     uint32_t total_n;
     const u128 total = cluster_sum(acc, n, &total_n);
     bool near;
@@ -994,6 +1079,93 @@ template <int DT> struct Row {
     return r;
   }
 
+  // ---- approximate sums ----
+  // Bounds on the exact sum of the FP64 weights exp(x) of the valid tokens
+  // `kept` accepts whose weight min-p keeps, i.e. on the oracle's fsum of
+  // that set before its rounding, from FP32 weights e = __expf(x32), each
+  // within MASS_ERR (1 + |x|) e of exact. A thread sums e and e |x| in FP32
+  // over at most eight groups (32 additions, each rounding by at most 2^-24
+  // of the partial sum, all terms being positive) before adding the partial
+  // sums into FP64. Tokens too close to the min-p threshold count only in
+  // the upper bound, as does 2^-120 for every counted token (an FP64 weight
+  // that the FP32 exponential flushes to zero). One exchange.
+  template <class Kept> __device__ Interval approx_mass(Kept kept, bool cuts) {
+    float s32 = 0.f, u32 = 0.f, ex32 = 0.f;  // weights kept, unsure; sum of e |x|
+    double s64 = 0, u64 = 0, ex64 = 0;
+    uint32_t n = 0;
+    int fold = 0;
+    const bool min_p_on = min_p > 0;
+    slice_pass([&](int g, const W* v, unsigned bits) {
+      if (!bits) return;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (!((bits >> j) & 1u)) continue;
+        if (cuts && !kept(order_key(v[j]), lo + 4 * g + j)) continue;
+        const float x = x32(v[j]);
+        if (!(x >= -746.f)) continue;  // exp(x) is 0 in FP64
+        bool sure = x > -744.f;
+        if (min_p_on) {
+          const float tol = __fadd_rn(__fmul_rn(X_ERR, fabsf(x)), mp_tol);
+          const float gap = __fsub_rn(x, ln_mp);
+          if (gap < -tol) continue;  // min-p certainly drops it
+          sure = sure && gap > tol;
+        }
+        const float e = __expf(x);
+        ex32 = __fmaf_rn(e, -x, ex32);
+        if (sure) s32 = __fadd_rn(s32, e);
+        else u32 = __fadd_rn(u32, e);
+        ++n;
+      }
+      if (++fold == 8) {
+        s64 += double(s32);
+        u64 += double(u32);
+        ex64 += double(ex32);
+        s32 = u32 = ex32 = 0.f;
+        fold = 0;
+      }
+    });
+    s64 += double(s32);
+    u64 += double(u32);
+    ex64 += double(ex32);
+    // This thread's error bound: the weights' own, and the FP32 additions'.
+    const double total = s64 + u64;
+    const double err = MASS_ERR * (total + ex64) * (1.0 + 0x1p-19) + 0x1p-19 * total + double(n) * 0x1p-120;
+    MassPart m{s64, u64, err, n};
+    auto merge = [](MassPart a, MassPart b) {
+      return MassPart{a.kept + b.kept, a.unsure + b.unsure, a.err + b.err, a.n + b.n};
+    };
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+      m = merge(m, MassPart{shfl_xor(m.kept, o), shfl_xor(m.unsure, o), shfl_xor(m.err, o), shfl_xor(m.n, o)});
+    if (lane_id() == 0) s.red.masses[warp_id()] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      MassPart b = s.red.masses[0];
+      for (int w = 1; w < WARPS; ++w) b = merge(b, s.red.masses[w]);
+      s.mass_part[parity()] = b;
+    }
+    exchange();
+    if (int(threadIdx.x) < ranks) s.peers.masses[threadIdx.x] = *peer(&s.mass_part[parity() ^ 1], threadIdx.x);
+    __syncthreads();
+    MassPart t = s.peers.masses[0];
+    for (int r = 1; r < ranks; ++r) t = merge(t, s.peers.masses[r]);
+    __syncthreads();
+    // FP64 additions of at most a few thousand partial sums: below 1e-12.
+    const double all = t.kept + t.unsure;
+    const double lo_ = t.kept - 1e-12 * t.kept - t.err;
+    const double hi_ = all + 1e-12 * all + t.err;
+    // The bounds' own FP64 roundings.
+    return Interval{lo_ * (1.0 - 0x1p-40), hi_ * (1.0 + 0x1p-40)};
+  }
+
+  // Rank 0 tells every rank a block-uniform decision (written into each
+  // rank's copy before the exchange, so no rank reads rank 0 afterwards).
+  __device__ bool broadcast_verdict(bool v) {
+    if (rank == 0 && int(threadIdx.x) < ranks) *peer(&s.verdict, threadIdx.x) = v ? 1 : 0;
+    exchange();
+    return s.verdict != 0;
+  }
+
   // ---- top-p over a full row ----
   // The shortest prefix of the kept set K (valid, cut_k, min-p) in (value
   // desc, ID asc) order whose correctly rounded sum reaches top_p * fsum(K):
@@ -1014,11 +1186,7 @@ template <int DT> struct Row {
         count[i] = 0;
       }
       __syncthreads();
-      for (int base = warp_id() * 32; base < groups; base += THREADS) {
-        const int g = base + lane_id();
-        W v[4];
-        unsigned bits = 0;
-        if (g < groups) bits = group(g, v);
+      slice_pass([&](int g, const W* v, unsigned bits) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           int d = -1;
@@ -1036,7 +1204,8 @@ template <int DT> struct Row {
           }
           warp_bucket_add(mass, count, d, f);
         }
-      }
+      });
+      ES_TRACE(p.workspace, p.rows, row, rank, shift == KEY_BITS - 8 ? 10 : 11);
       exchange();
       // Thread i owns digit 255 - i: merged mass and count, scanned from the top.
       u128 m = 0;
@@ -1117,7 +1286,9 @@ template <int DT> struct Row {
   // (and min-p keeps), except `excluded`; an FP64 rescore of every token
   // whose bound reaches the FP32 winner's lower bound when the certificate
   // fails (or of every token, with exact_only). Returns -1 if none is kept.
-  template <class Kept> __device__ int draw(uint32_t sub, int excluded, Kept kept, bool exact_only) {
+  // `cuts`: `kept` rejects tokens (a top-k or top-p cut is on), so it is
+  // applied before the Philox words are made.
+  template <class Kept> __device__ int draw(uint32_t sub, int excluded, Kept kept, bool cuts, bool exact_only) {
     // A kept token's score bounds the winner's from below: the maximum
     // (x = 0), unless it is excluded.
     const int greedy = argmax_id();
@@ -1140,30 +1311,63 @@ template <int DT> struct Row {
     Pick best = no_pick();
     float skipped = -INFINITY;
     if (!exact_only) {
-      for (int g = threadIdx.x; g < groups; g += THREADS) {
-        W v[4];
-        const unsigned bits = group(g, v);
+      // Screens, from cheap to exact, against bar = the best lower bound so
+      // far (or the floor) less PRUNE_MARGIN. A token screened out has an
+      // upper bound below the bar, so `skipped` takes the bar itself: below
+      // the winner's lower bound by the margin, it never blocks the
+      // certificate. The screens' own FP32 roundings (about 1e-5) are
+      // covered by slacks of 1e-3 and 1e-4.
+      //
+      slice_pass([&](int g, const W* v, unsigned bits) {
+        if (!bits) return;
+        const float bar = fmaxf(floor, best.lo) - PRUNE_MARGIN;
+        // 1. Value: x + NOISE_MAX + SCORE_ERR (1 + |x| + NOISE_MAX) < bar,
+        //    i.e. (x <= 0) x < (bar - LIVE_OFFSET) / (1 - SCORE_ERR).
+        const float x_live = __fsub_rn(__fmul_rn(__fsub_rn(bar, LIVE_OFFSET), 1.f + 2.f * SCORE_ERR), 1e-3f);
         float xs[4];
         unsigned live = 0;
-        const float bar = fmaxf(floor, best.lo) - PRUNE_MARGIN;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const int t = lo + 4 * g + j;
-          xs[j] = 0.f;
-          if (!((bits >> j) & 1u) || t == excluded) continue;
-          const float x = x32(v[j]);
-          if (!kept(order_key(v[j]), t) || !weight_kept(v[j], x)) continue;
-          xs[j] = x;
-          const float ub = x + NOISE_MAX + SCORE_ERR * (1.f + fabsf(x) + NOISE_MAX);
-          if (ub >= bar) live |= 1u << j;
-          else skipped = fmaxf(skipped, ub);
+          xs[j] = x32(v[j]);
+          if (((bits >> j) & 1u) && xs[j] >= x_live && (!cuts || kept(order_key(v[j]), lo + 4 * g + j)))
+            live |= 1u << j;
         }
-        if (!live) continue;
+        if (live != bits) skipped = fmaxf(skipped, bar);
+        if (!live) return;
         const Words r = addr.group(sub, uint32_t((lo >> 2) + g));
+        // 2. Noise, integers only: G(w) <= (clz(~w) + 1) ln 2, since
+        //    -log(u) >= 1 - u >= 2^-(clz(~w) + 1); first for the group (its
+        //    largest live x with its largest bound), then per token.
+        auto cheap_ub = [](float x, int l) {
+          const float gn = __fmul_rn(float(l + 1), LN2_UP);
+          return __fadd_rn(__fadd_rn(__fmul_rn(x, 1.f - SCORE_ERR), __fmul_rn(gn, 1.f + SCORE_ERR)), SCORE_ERR + 1e-4f);
+        };
+        int lz[4], lmax = 0;
+        float xmax = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          lz[j] = __clz(~r.w[j]);
+          if ((live >> j) & 1u) {
+            lmax = max(lmax, lz[j]);
+            xmax = fmaxf(xmax, xs[j]);
+          }
+        }
+        if (cheap_ub(xmax, lmax) < bar) {
+          skipped = fmaxf(skipped, bar);
+          return;
+        }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           if (!((live >> j) & 1u)) continue;
           const float x = xs[j];
+          if (cheap_ub(x, lz[j]) < bar) {
+            skipped = fmaxf(skipped, bar);
+            continue;
+          }
+          // 3. The rare token that might still win: exact membership, a
+          //    tighter noise bound, then the certified FP32 score.
+          const int t = lo + 4 * g + j;
+          if (t == excluded || (!cuts && !kept(order_key(v[j]), t)) || !weight_kept(v[j], x)) continue;
           const float gu = noise_upper(r.w[j]);
           const float ub = x + gu + SCORE_ERR * (1.f + fabsf(x) + fabsf(gu));
           if (ub < fmaxf(floor, best.lo) - PRUNE_MARGIN) {
@@ -1173,10 +1377,11 @@ template <int DT> struct Row {
           const float G = noise32(r.w[j]);
           const float sc = __fadd_rn(x, G);
           const float err = SCORE_ERR * (1.f + fabsf(x) + fabsf(G));
-          best = pick_of(best, Pick{sc, sc - err, sc + err, -INFINITY, lo + 4 * g + j});
+          best = pick_of(best, Pick{sc, sc - err, sc + err, -INFINITY, t});
         }
-      }
+      });
     }
+    ES_TRACE(p.workspace, p.rows, row, rank, 13);
     best.others = fmaxf(best.others, skipped);
     best = block_all(best, [](Pick a, Pick b) { return pick_of(a, b); }, s.red.picks);
     if (threadIdx.x == 0) s.pick[parity()] = best;
@@ -1191,6 +1396,7 @@ template <int DT> struct Row {
       if (top.lo > top.others) return top.id;
       count_fallback();
     }
+    ES_TRACE(p.workspace, p.rows, row, rank, 14);
     // FP64: every kept token whose upper bound reaches the threshold.
     const float threshold = exact_only ? -INFINITY : top.lo;
     Best b = no_best();

@@ -89,6 +89,26 @@ def test_benchmark_configuration_full_size(name):
         assert (expected[2] == 2).all()  # coupled mode with full proposals is invalid by contract
 
 
+@pytest.mark.parametrize("setting", ["qwen", "temperature", "top_p"])
+def test_sampler_grid_settings(setting):
+    """The three settings of the reference's sampler benchmark grid
+    (bench/sampler.py:36-41) on bf16 rows: sampling rows, and ratio
+    verification whose draft rows need the kept set's mass (temperature
+    only: bounds on it settle most tests; top-p only: a list of the largest
+    tokens settles the nucleus), against the oracle."""
+    import bench
+    chosen = bench.SAMPLER_SETTINGS[setting]
+    for w in [workloads.sampling(8, chosen, master_seed=61), workloads.verification(6, 4, chosen, master_seed=62)]:
+        case = dict(name=f"{setting}_{w.name}", logits=C.round_to(w.logits, "bfloat16"), cu_rows=w.cu_rows,
+                    draft_ids=w.draft_ids, temperature=w.temperature, top_k=w.top_k, top_p=w.top_p, min_p=w.min_p,
+                    draft_kind=w.draft_kind, seed=w.seed, stream_id=w.stream_id, positions=w.positions, mask=None,
+                    draft_logits=None, mode="ratio", logit_dtype="bfloat16")
+        expected = oracle_outputs(case)
+        for list_max in [256, 0]:
+            got = run_abi(device_inputs(case), list_max=list_max)
+            assert_same(got, expected, context=f"{case['name']} list_max={list_max}")
+
+
 def test_temperature_only_batch_sizes_and_slot_permutation():
     case = C.workload_case("C2b")
     expected = oracle_outputs(case)
