@@ -2,9 +2,10 @@
 //
 // Each of the cluster's C blocks ("ranks") owns a contiguous slice of the
 // row (a multiple of 32 tokens, so slices align with mask words and with the
-// Philox groups of four) and copies it once from HBM into its shared memory
-// with TMA bulk copies. Every later pass over the row (statistics, windows,
-// selections, sums, draws, FP64 rescoring) reads shared memory, and the ranks
+// Philox groups of four). Small batches copy the slice once from HBM into
+// shared memory with TMA bulk copies, and every pass reads it there; larger
+// batches stream it through a ring of TMA stages, once for the statistics
+// and again for each later whole-row pass (mostly from L2). The ranks
 // combine partial results through distributed shared memory after a cluster
 // barrier. Each rank merges the C partial results itself, in rank order, so
 // every rank holds bitwise the same row-level values and takes the same
@@ -24,7 +25,10 @@
 //     token (FP32 with a margin, FP64 near the threshold); top-p by a radix
 //     selection weighted by FP64 weights summed exactly in 128-bit fixed
 //     point, i.e. the oracle's correctly rounded math.fsum;
-//   * normalizers and the ratio test: FP64 on exact sums, as in the oracle;
+//   * normalizers and the ratio test: FP64 on exact sums, as in the oracle,
+//     or bounds on a sum where every value within them gives the same
+//     decision (a top-p boundary, a ratio test): FP32 sums with an error
+//     bound, the exact sum only when the bounds leave the decision open;
 //   * draws over lists (at most 256 tokens): the oracle's FP64 log(p) + G;
 //     over larger kept sets: a certified FP32 argmax of x + G with an FP64
 //     rescore of every token that could still win.
