@@ -82,3 +82,19 @@ def test_reference_arm_under_torchrun_prints_one_line():
     line = json.loads(lines[0])
     assert line["impl"] == "reference" and line["n_gpus"] == 2 and line["value"] > 0
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["cpu_baseline"]["kind"] == "port"
+
+
+def test_sampler_grid_is_the_reference_grid():
+    """bench.py --sampler-shapes runs the grid of the reference's
+    bench/sampler.py:36-41: three settings by eight (requests, drafts) shapes."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    assert bench.SAMPLER_SETTINGS == {
+        "qwen": dict(temperature=0.6, top_k=20, top_p=0.95, min_p=0.0),
+        "temperature": dict(temperature=1.0, top_k=0, top_p=1.0, min_p=0.0),
+        "top_p": dict(temperature=0.7, top_k=0, top_p=0.9, min_p=0.0),
+    }
+    assert bench.SAMPLER_SHAPES == [(1, 0), (8, 0), (32, 0), (128, 0), (1, 4), (8, 4), (32, 4), (64, 4)]
+    done = _bench(["bench.py", "--sampler-shapes", "nonsense"], {})
+    assert done.returncode != 0 and "invalid choice" in done.stderr
