@@ -45,8 +45,16 @@ def test_max_over_ranks_with_two_gloo_ranks():
 
     values = [[103.0, 7.5, 1.0], [99.0, 9.25, 2.0]]
     with mp.Manager() as manager:
-        results = manager.dict()
-        mp.spawn(_max_worker, args=(2, _free_port(), values, results), nprocs=2, join=True)
+        # A free port can be taken by another process before rank 0 binds it:
+        # such an attempt fails at rendezvous and is retried on a new port.
+        for attempt in range(3):
+            results = manager.dict()
+            try:
+                mp.spawn(_max_worker, args=(2, _free_port(), values, results), nprocs=2, join=True)
+                break
+            except mp.ProcessRaisedException as e:
+                if attempt == 2 or "address already in use" not in str(e).lower():
+                    raise
         got = dict(results)
     assert got[0] == got[1] == [103.0, 9.25, 2.0]
 
