@@ -299,6 +299,8 @@ def decode_step(logits, offsets, row_tokens, positions, *, staging: StepStaging,
     mask = None
     if grammar is not None and len(grammar[1]):
         req_ids, grammar_req_ids, bitmask = grammar
+        if mask_buffer is None or mask_buffer.shape[0] < rows:
+            raise DecodeStepError("a grammar needs a mask_buffer with a row per logits row")
         sources = grammar_row_sources(req_ids, offsets_np, grammar_req_ids, int(bitmask.shape[0]))
         mask = densify_grammar_mask(bitmask, sources, mask_buffer[:rows])
     rng = CudaRngKey(step.seeds, streams, positions.to(torch.int64))
