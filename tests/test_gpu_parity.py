@@ -109,6 +109,22 @@ def test_sampler_grid_settings(setting):
             assert_same(got, expected, context=f"{case['name']} list_max={list_max}")
 
 
+@pytest.mark.parametrize("vocab", range(1, 9))
+def test_every_mask_of_a_uniform_row(vocab):
+    """Every nonempty mask of a uniform row, with top-k 0, 1 or V and top-p
+    1/4 ... 1, one request each (all tokens tie, so the kept set and the
+    draw turn on ID order alone), against the oracle, with lists on and off."""
+    combos = [(bits, k, p) for bits in range(1, 1 << vocab) for k in [0, 1, vocab] for p in [0.25, 0.5, 0.75, 1.0]]
+    n = len(combos)
+    case = C._case(f"masks_{vocab}", np.zeros((n, vocab)), np.arange(n + 1), np.empty((n, 0), np.int64),
+                   top_k=[k for _, k, _ in combos], top_p=[p for _, _, p in combos],
+                   seed=list(range(500, 500 + n)), mask=np.array([[bits] for bits, _, _ in combos], np.int32),
+                   logit_dtype="float32")
+    expected = oracle_outputs(case)
+    for list_max in [256, 0]:
+        assert_same(run_abi(device_inputs(case), list_max=list_max), expected, context=f"list_max={list_max}")
+
+
 def test_temperature_only_batch_sizes_and_slot_permutation():
     case = C.workload_case("C2b")
     expected = oracle_outputs(case)

@@ -93,3 +93,23 @@ def test_large_golden(entry):
     np.testing.assert_array_equal(out.status, status)
     np.testing.assert_array_equal(out.tokens, tokens)
     np.testing.assert_array_equal(out.accepted_len, accepted)
+
+
+def test_every_mask_of_a_uniform_row():
+    """Every nonempty mask of uniform rows of 1 to 8 tokens, with top-k 0, 1 or
+    V and top-p 1/4 ... 1: the kept set is the first ceil(kept * top_p)
+    allowed IDs (ties break by ID), each with mass exactly 1/n (the
+    reference's tests/exact/test_exhaustive_oracle.py:12-27 check)."""
+    for vocab in range(1, 9):
+        for bits in range(1, 1 << vocab):
+            allowed = [t for t in range(vocab) if bits >> t & 1]
+            for k in [0, 1, vocab]:
+                kept = len(allowed) if k == 0 else min(k, len(allowed))
+                for top_p in [0.25, 0.5, 0.75, 1.0]:
+                    n = math.ceil(kept * top_p)
+                    expected = np.zeros(vocab)
+                    expected[allowed[:n]] = 1 / n
+                    probs, status = oracle.distribution(np.zeros(vocab), top_k=k, top_p=top_p,
+                                                        mask=np.array([bits], np.int32))
+                    assert status == oracle.Status.OK
+                    np.testing.assert_array_equal(probs, expected)
