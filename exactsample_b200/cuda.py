@@ -1,16 +1,18 @@
-"""Allocation-free CUDA decode calls with explicit, reusable workspace ownership.
+"""The device-side decode API: ``plan`` once, then ``verify`` every step.
 
-Drop-in for the reference's ``exactsample.cuda`` module
-(python/exactsample/cuda.py:15-198): the same dataclasses, ``plan`` /
-``CudaPlan`` / ``verify`` signatures, the same torch op
-``torch.ops.exactsample.verify_out`` (schema of csrc/bindings.cpp:139-146) and
-the same exception types and messages, so callers such as a vLLM bridge work
-unchanged. Behind the op are the B200 kernels of ``libexactsample_b200.so``
-(through its C ABI, include/exactsample_b200.h).
+This module replaces the reference's ``exactsample.cuda``
+(python/exactsample/cuda.py:15-198) for callers such as a vLLM bridge: its
+dataclasses, the signatures of ``plan`` / ``CudaPlan`` / ``verify``, the torch
+op ``torch.ops.exactsample.verify_out`` (schema of csrc/bindings.cpp:139-146),
+and its exception types and messages are kept. The op runs the B200 kernels of
+``libexactsample_b200.so`` through that library's C ABI
+(include/exactsample_b200.h).
 
-Creating a plan, outputs and parameter tensors is setup; ``verify`` only uses
-existing device tensors and never copies parameters from the host. There is
-no CPU fallback: a missing native library raises.
+A plan owns one workspace; the caller owns every input and output tensor and
+makes them before the first step. A step (``verify``) launches kernels on
+tensors that already live on the device: it neither allocates nor reads
+anything from the host. If the native library is missing, the call raises;
+nothing falls back to the CPU.
 """
 from __future__ import annotations
 
@@ -119,11 +121,15 @@ class _Ownership:
 
 
 class CudaPlan:
-    """One workspace. Calls on one stream queue safely; concurrent streams fail.
+    """A workspace sized for ``max_rows`` rows and its ownership rules.
 
-    Inputs and outputs must not be mutated until ``synchronize`` or normal CUDA
-    stream ordering establishes completion. Tensor allocator lifetimes are
-    recorded on the consuming stream.
+    Calls queued on one stream run in order. A call from a second stream while
+    the previous call is still running raises instead of racing on the
+    workspace. A call's tensors belong to it until it has finished on the
+    device (``synchronize``, or any later work on the same stream), so the
+    caller must not overwrite them before then; each tensor is recorded on
+    the launching stream, so the caching allocator cannot hand its memory to
+    someone else early.
 
     CUDA graph capture is refused, as in the reference, unless the plan is
     made with ``graphs=True``: ``verify`` then may be captured (it allocates
@@ -171,14 +177,16 @@ class CudaPlan:
                           ints(self.max_requests), ints(self.max_requests))
 
     def fallbacks(self) -> int:
-        """FP64 recomputations made by the fused path in the last call (synchronizes)."""
+        """How many times the last call had to settle a draw or a cut in FP64
+        because the FP32 bounds left it open. Waits for that call to finish."""
         import torch
 
         self.synchronize()
         return int(self.workspace[4:8].view(torch.int32).item())
 
     def synchronize(self) -> None:
-        """Wait for this plan's last call, allowing workspace reuse on any stream."""
+        """Blocks until this plan's last call has finished; after that any
+        stream may use the workspace."""
         self._owner.drain()
 
 
@@ -212,13 +220,17 @@ def verify(target_logits, cu_rows, draft_ids, *, params: CudaRequestParams,
            rng: CudaRngKey, plan: CudaPlan, out: CudaOutput,
            draft_logits=None, mask=None, mode: str = "ratio", dispatch: str = "auto",
            top_k_top_p: bool = True) -> CudaOutput:
-    """Verify ragged proposals in existing buffers and return ``out``.
+    """Samples or verifies a ragged batch and writes the results into ``out``.
 
-    All inputs must already be CUDA tensors. ``draft_logits`` are log weights of
-    the *actual* proposal distribution, after its own processors and filters;
-    no target filters are applied to q. Bonus q rows are ignored. Only the first
-    ``out.num_requests`` output rows belong to the call; capacity tails are not
-    touched. Invalid device values yield a per-request status asynchronously.
+    Request i owns rows ``cu_rows[i]:cu_rows[i + 1]`` of ``target_logits``:
+    one row per draft token plus a final bonus row. Every tensor must already
+    be on the plan's device. ``draft_logits`` (full-q drafts only) give the
+    log weights of the distribution the drafter really sampled from, with its
+    own processing already applied; the target's filters are not applied to
+    them, and the bonus rows' entries are not read. The call writes output
+    rows ``0 .. out.num_requests - 1`` and leaves the rest of ``out`` alone.
+    Bad values inside device tensors (NaN logits, an out-of-range parameter)
+    do not raise: they show up later as that request's status.
 
     ``top_k_top_p=False`` tells the kernels that no request has a top-k below
     the vocabulary or a top-p below 1 (a caller that keeps its sampling

@@ -1,75 +1,139 @@
-// Exhaustive check of the FP32 Gumbel noise used by the row kernel's
-// certified draws, over all 2^32 Philox words:
+// Exhaustive check, on the GPU, of the three facts about the FP32 Gumbel
+// noise that the row kernel's certified draws rest on. For every 32-bit
+// Philox word w, with G(w) = -log(-log u), u = (w + 0.5) / 2^32, computed in
+// FP64 (log1p of the exact complement for u >= 1/2):
 //
-//   |noise32(w) - G(w)| <= NOISE_ERR * (1 + |G(w)|)   (the bound the draws assume)
-//   noise_upper(w) >= G(w)                           (the pruning screen is an upper bound)
-//   G(w) <= NOISE_MAX                                (the noise ceiling of the first screen)
+//   (1) |noise32(w) - G(w)| <= NOISE_ERR * (1 + |G(w)|)
+//   (2) noise_upper(w) >= G(w)
+//   (3) G(w) <= NOISE_MAX
 //
-// G(w) = -log(-log u), u = (w + 0.5) / 2^32, in FP64 with log1p above u = 1/2.
-// Built with the library's flags (--fmad=false) by tests/noise_bounds.py;
-// prints one JSON line and exits 0 iff every check holds.
+// Layout: the 2^32 words are cut into 2^16 pages of 2^16 words; blocks take
+// pages in turn. Each thread keeps its findings in registers, each block
+// folds them in shared memory, and one thread per block folds the block's
+// summary into a single device record with atomics. The report is a
+// histogram of the error as a fraction of its bound (eighths, last bucket
+// above the bound), the worst word, the smallest screen margin and the
+// noise range. Built with the library's flags (--fmad=false) by
+// tests/noise_bounds.py; prints one JSON line, exit status 0 iff all three
+// hold for every word.
 #include <cstdio>
-#include <vector>
+#include <cstring>
 
 #include "../exactsample_b200/csrc/es_device.cuh"
 
 namespace {
-constexpr int BLOCKS = 148 * 16, THREADS = 256;
 
-struct Stats {
-  double worst_ratio, min_margin, max_g, min_g;
-  unsigned long long violations, screen_violations;
-  unsigned worst_word;
+constexpr int PAGE_BITS = 16;
+constexpr unsigned PAGES = 1u << (32 - PAGE_BITS);
+constexpr int BLOCK = 512;
+constexpr int BUCKETS = 9;  // error / bound in [k/8, (k+1)/8) for k < 8; bucket 8: above the bound
+
+// Order-preserving 64-bit keys of doubles, so that atomicMax / atomicMin on
+// integers track a maximum or minimum double.
+__device__ unsigned long long up_key(double x) {
+  const unsigned long long b = static_cast<unsigned long long>(__double_as_longlong(x));
+  return (b >> 63) ? ~b : (b | (1ull << 63));
+}
+double from_key(unsigned long long k) {
+  const unsigned long long b = (k >> 63) ? (k & ~(1ull << 63)) : ~k;
+  double x;
+  std::memcpy(&x, &b, sizeof x);
+  return x;
+}
+
+struct Record {
+  unsigned long long bucket[BUCKETS];
+  unsigned long long worst;       // (float bits of error/bound) << 32 | word: the largest ratio
+  unsigned long long min_margin;  // up_key of the smallest noise_upper - G
+  unsigned long long screen_failures;
+  unsigned long long max_noise, min_noise;  // up_key of the noise range
 };
 
-__device__ double reference_noise(uint32_t w) {
-  const double e = w < 0x80000000u ? -log((double(w) + 0.5) * 0x1p-32) : -log1p(-(double(~w) + 0.5) * 0x1p-32);
-  return -log(e);
+__device__ double exact_noise(uint32_t w) {
+  const double minus_log_u = w < 0x80000000u ? -log((double(w) + 0.5) * 0x1p-32)
+                                             : -log1p(-(double(~w) + 0.5) * 0x1p-32);
+  return -log(minus_log_u);
 }
 
-__global__ void check(Stats* out) {
-  Stats s{0., 1e300, -1e300, 1e300, 0, 0, 0};
-  const uint64_t stride = uint64_t(BLOCKS) * THREADS;
-  for (uint64_t i = uint64_t(blockIdx.x) * THREADS + threadIdx.x; i < (1ull << 32); i += stride) {
-    const uint32_t w = uint32_t(i);
-    const double g = reference_noise(w);
-    const double ratio = fabs(double(es::noise32(w)) - g) / (double(es::NOISE_ERR) * (1. + fabs(g)));
-    if (ratio > s.worst_ratio) { s.worst_ratio = ratio; s.worst_word = w; }
-    s.violations += ratio > 1.;
-    const double margin = double(es::noise_upper(w)) - g;
-    s.min_margin = fmin(s.min_margin, margin);
-    s.screen_violations += margin < 0.;
-    s.max_g = fmax(s.max_g, g);
-    s.min_g = fmin(s.min_g, g);
+__global__ void __launch_bounds__(BLOCK) sweep(Record* out) {
+  __shared__ unsigned long long s_bucket[BUCKETS];
+  __shared__ unsigned long long s_worst, s_margin, s_screen, s_max, s_min;
+  if (threadIdx.x < BUCKETS) s_bucket[threadIdx.x] = 0;
+  if (threadIdx.x == 0) {
+    s_worst = 0;
+    s_margin = ~0ull;
+    s_screen = 0;
+    s_max = 0;
+    s_min = ~0ull;
   }
-  out[blockIdx.x * THREADS + threadIdx.x] = s;
+  __syncthreads();
+  unsigned long long bucket[BUCKETS] = {};
+  unsigned long long worst = 0, margin = ~0ull, screen = 0, gmax = 0, gmin = ~0ull;
+  for (unsigned page = blockIdx.x; page < PAGES; page += gridDim.x) {
+    for (unsigned k = threadIdx.x; k < (1u << PAGE_BITS); k += BLOCK) {
+      const uint32_t w = (page << PAGE_BITS) | k;
+      const double g = exact_noise(w);
+      const double ratio = fabs(double(es::noise32(w)) - g) / (double(es::NOISE_ERR) * (1.0 + fabs(g)));
+      ++bucket[ratio > 1.0 ? BUCKETS - 1 : min(int(ratio * 8.0), BUCKETS - 2)];
+      const unsigned long long tagged =
+          (static_cast<unsigned long long>(__float_as_uint(float(ratio))) << 32) | w;
+      worst = tagged > worst ? tagged : worst;
+      const double gap = double(es::noise_upper(w)) - g;
+      screen += gap < 0.0;
+      const unsigned long long gk = up_key(gap), nk = up_key(g);
+      margin = gk < margin ? gk : margin;
+      gmax = nk > gmax ? nk : gmax;
+      gmin = nk < gmin ? nk : gmin;
+    }
+  }
+  for (int b = 0; b < BUCKETS; ++b)
+    if (bucket[b]) atomicAdd(&s_bucket[b], bucket[b]);
+  atomicMax(&s_worst, worst);
+  atomicMin(&s_margin, margin);
+  if (screen) atomicAdd(&s_screen, screen);
+  atomicMax(&s_max, gmax);
+  atomicMin(&s_min, gmin);
+  __syncthreads();
+  if (threadIdx.x < BUCKETS) atomicAdd(&out->bucket[threadIdx.x], s_bucket[threadIdx.x]);
+  if (threadIdx.x == 0) {
+    atomicMax(&out->worst, s_worst);
+    atomicMin(&out->min_margin, s_margin);
+    atomicAdd(&out->screen_failures, s_screen);
+    atomicMax(&out->max_noise, s_max);
+    atomicMin(&out->min_noise, s_min);
+  }
 }
+
 }  // namespace
 
 int main() {
-  const int n = BLOCKS * THREADS;
-  Stats* device = nullptr;
-  if (cudaMalloc(&device, n * sizeof(Stats)) != cudaSuccess) return 2;
-  check<<<BLOCKS, THREADS>>>(device);
-  if (cudaDeviceSynchronize() != cudaSuccess) return 2;
-  std::vector<Stats> host(n);
-  if (cudaMemcpy(host.data(), device, n * sizeof(Stats), cudaMemcpyDeviceToHost) != cudaSuccess) return 2;
-  cudaFree(device);
-  Stats t = host[0];
-  t.violations = t.screen_violations = 0;
-  for (const Stats& s : host) {
-    if (s.worst_ratio > t.worst_ratio) { t.worst_ratio = s.worst_ratio; t.worst_word = s.worst_word; }
-    t.min_margin = s.min_margin < t.min_margin ? s.min_margin : t.min_margin;
-    t.max_g = s.max_g > t.max_g ? s.max_g : t.max_g;
-    t.min_g = s.min_g < t.min_g ? s.min_g : t.min_g;
-    t.violations += s.violations;
-    t.screen_violations += s.screen_violations;
-  }
-  const bool pass = t.violations == 0 && t.screen_violations == 0 && t.max_g <= double(es::NOISE_MAX);
-  std::printf("{\"words\": 4294967296, \"noise_err\": %.3g, \"worst_error_over_bound\": %.6f, \"worst_word\": %u, "
-              "\"error_violations\": %llu, \"screen_min_margin\": %.9g, \"screen_violations\": %llu, "
-              "\"max_noise\": %.9f, \"min_noise\": %.9f, \"noise_max\": %.6f, \"passed\": %s}\n",
-              double(es::NOISE_ERR), t.worst_ratio, t.worst_word, t.violations, t.min_margin, t.screen_violations,
-              t.max_g, t.min_g, double(es::NOISE_MAX), pass ? "true" : "false");
+  Record init{};
+  init.min_margin = ~0ull;
+  init.min_noise = ~0ull;
+  Record* dev = nullptr;
+  if (cudaMalloc(&dev, sizeof(Record)) != cudaSuccess) return 2;
+  if (cudaMemcpy(dev, &init, sizeof init, cudaMemcpyHostToDevice) != cudaSuccess) return 2;
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+  sweep<<<4 * (sms > 0 ? sms : 148), BLOCK>>>(dev);
+  Record r{};
+  if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpy(&r, dev, sizeof r, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return 2;
+  cudaFree(dev);
+  unsigned long long words = 0;
+  for (unsigned long long b : r.bucket) words += b;
+  const unsigned worst_bits = unsigned(r.worst >> 32);
+  float worst_ratio;
+  std::memcpy(&worst_ratio, &worst_bits, sizeof worst_ratio);
+  const double max_noise = from_key(r.max_noise), min_noise = from_key(r.min_noise);
+  const bool pass = words == (1ull << 32) && r.bucket[BUCKETS - 1] == 0 && r.screen_failures == 0 &&
+                    max_noise <= double(es::NOISE_MAX);
+  std::printf("{\"words\": %llu, \"noise_err\": %.3g, \"error_over_bound_eighths\": [", words, double(es::NOISE_ERR));
+  for (int b = 0; b < BUCKETS; ++b) std::printf("%s%llu", b ? ", " : "", r.bucket[b]);
+  std::printf("], \"error_violations\": %llu, \"worst_error_over_bound\": %.6f, \"worst_word\": %u, "
+              "\"screen_violations\": %llu, \"screen_min_margin\": %.9g, \"max_noise\": %.9f, \"min_noise\": %.9f, "
+              "\"noise_max\": %.6f, \"passed\": %s}\n",
+              r.bucket[BUCKETS - 1], double(worst_ratio), unsigned(r.worst & 0xffffffffu), r.screen_failures,
+              from_key(r.min_margin), max_noise, min_noise, double(es::NOISE_MAX), pass ? "true" : "false");
   return pass ? 0 : 1;
 }
