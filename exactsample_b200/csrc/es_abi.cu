@@ -437,6 +437,12 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
   p.exact_draws = a->dispatch == ES_REFERENCE;
   p.list_max = p.exact_draws ? 0 : int32_t(a->list_max);
   p.offsets_inline = requests <= 8192;
+  p.fast = !p.exact_draws && p.list_max > 0 && sh == nullptr;
+  p.warm = p.fast;
+  if (const char* forced = std::getenv("EXACTSAMPLE_FAST")) {  // 0: the block-level list path only; 1: no warm-up warp
+    if (forced[0] == '0') p.fast = p.warm = 0;
+    if (forced[0] == '1') p.warm = 0;
+  }
   if (sh != nullptr) {
     es::Shards& t = p.sh;
     t.count = sh->count;

@@ -232,6 +232,22 @@ template <class T, class Op> __device__ __forceinline__ T block_all(T v, Op op, 
   __syncthreads();
   return r;
 }
+// Barrier 1 over the block's first THREADS threads only (the row's warps):
+// an extra warp outside them (the row kernel's warm-up warp) never holds
+// them up. The _or form also ORs a predicate over those threads.
+__device__ __forceinline__ void sync_rows() { asm volatile("bar.sync 1, %0;" ::"n"(THREADS) : "memory"); }
+__device__ __forceinline__ bool sync_rows_or(bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred a, b;\n\t"
+      "setp.ne.u32 a, %1, 0;\n\t"
+      "bar.red.or.pred b, 1, %2, a;\n\t"
+      "selp.u32 %0, 1, 0, b;\n\t}"
+      : "=r"(r)
+      : "r"(uint32_t(p)), "n"(THREADS)
+      : "memory");
+  return r != 0;
+}
 // Inclusive prefix sum over the block in thread order; *total gets the sum.
 template <class T> __device__ __forceinline__ T block_scan(T v, T* scratch, T* total) {
 #pragma unroll

@@ -277,9 +277,64 @@ template <int DT> struct RowKernel {
     return true;
   }
 
+  // The warp-level list path (es_fast.cuh) for a top-k of n_keep <=
+  // FAST_KEEP tokens: the window from the tile-maximum bins merged with the
+  // statistics, the gather by every warp over its share of the rank's tiles
+  // into rank 0's candidate buffer, one exchange, and rank 0's warp finish
+  // (or its block finish when more than FAST_CAND candidates arrived).
+  // Returns true when the row is finished on rank 0 (no rank reads another's
+  // memory afterwards); false, the same on every rank, when it does not
+  // apply (no window in WIN_BINS bins, or more than CAP candidates).
+  __device__ static bool fast_list(R& r, const RowCtx& c, int n_keep, bool verify, RowResult& res, const Params& p) {
+    auto& s = r.s;
+    if (warp_id() == 0) {
+      const int j = window_warp(s.win, n_keep);
+      if (lane_id() == 0) s.ival[0] = j;
+    }
+    __syncthreads();
+    const int j = s.ival[0];
+    ES_TRACE(p.workspace, p.rows, r.row, r.rank, 4);
+    if (j < 0) return false;
+    const int bin = r.top_bin - j;
+    const SliceRef<T> src =
+        r.resident ? SliceRef<T>{r.slice, 1, r.has_mask ? reinterpret_cast<const int32_t*>(r.mask_s) : nullptr, 1,
+                                 r.hi - r.lo, r.lo}
+                   : SliceRef<T>{r.tbase + int64_t(r.lo) * p.t_s1, p.t_s1,
+                                 r.has_mask ? p.mask + int64_t(r.row) * p.m_s0 + int64_t(r.lo >> 5) * p.m_s1 : nullptr,
+                                 p.m_s1, r.hi - r.lo, r.lo};
+    const int nt = r.tile_count();
+    const int per = (nt + WARPS - 1) / WARPS;
+    const int t0 = min(nt, warp_id() * per), t1 = min(nt, t0 + per);
+    int mine = gather_warp<T, W>(src, r.tmax, t0, t1, bin, r.peer(s.u.cand.key, 0), r.peer(s.u.cand.id, 0),
+                                 r.peer(&s.n_cand, 0), CAP);
+    mine = block_all(lane_id() == 0 ? mine : 0, [](int x, int y) { return x + y; }, s.red.ints);
+    if (int(threadIdx.x) < r.ranks) r.peer(s.pushed, threadIdx.x)[r.rank] = mine;
+    ES_TRACE(p.workspace, p.rows, r.row, r.rank, 14);
+    r.exchange();
+    ES_TRACE(p.workspace, p.rows, r.row, r.rank, 5);
+    int m = 0;
+    for (int rr = 0; rr < r.ranks; ++rr) m += s.pushed[rr];
+    if (m > CAP) return false;  // the block path's radix selection decides
+    if (r.rank != 0) return true;
+    if (m <= FAST_CAND) {
+      if (warp_id() == 0) {
+        const ListIn in{s.u.cand.key, s.u.cand.id, m, n_keep, double(r.maxv), r.temperature, r.min_p, r.top_p,
+                        r.addr, verify ? 1 : 0, c.draft_id, &diagnostics(p.workspace, p.rows)->near_ties};
+        const ListOut o = finish_warp<W>(in);
+        res.sample = o.sample;
+        res.accept = o.accept;
+        res.residual = o.residual;
+      }
+      ES_TRACE(p.workspace, p.rows, r.row, r.rank, 12);
+    } else {
+      list_finish(r, c, m, n_keep, verify, false, 0.0, res, Interval{0, 0});
+    }
+    return true;
+  }
+
   // Returns true when rank 0 finishes the row alone (a list row): the other
   // ranks may then exit, since no rank touches another's memory afterwards.
-  __device__ static bool positive(R& r, const RowCtx& c, bool verify, bool full_q, double sq, RowResult& res,
+  __device__ __forceinline__ static bool positive(R& r, const RowCtx& c, bool verify, bool full_q, double sq, RowResult& res,
                                   const Params& p) {
     const int valid = r.all.valid;
     const int64_t k = c.top_k;
@@ -292,6 +347,9 @@ template <int DT> struct RowKernel {
     // selection below decides when neither list settles the boundary.
     const bool list_row = n_keep <= list_max;
     const bool top_p_list = !list_row && n_keep == valid && r.top_p < 1 && list_max > 0;
+    if (list_row && n_keep < valid && n_keep <= FAST_KEEP && p.fast && !full_q && r.top_bin >= 0 &&
+        fast_list(r, c, n_keep, verify, res, p))
+      return true;
     Interval target{0, 0};
     if (top_p_list) {
       const Interval total = r.approx_mass([](Key, int) { return true; }, false);
@@ -372,10 +430,48 @@ template <int DT> struct RowKernel {
   }
 };
 
+// The warm-up warp (es_fast.cuh): the warp-level list steps once on dummy
+// data in the block's FP64 list arrays, which no list uses before the first
+// cluster exchange, and that exchange cannot complete before this warp has
+// exited. Writes nothing else.
+template <int DT> __device__ void warm_up(Smem<typename Types<DT>::W>& s) {
+  using T = typename Types<DT>::T;
+  using W = typename Types<DT>::W;
+  struct Dry {
+    T row[64];
+    W tmax[2];
+    uint32_t counts[WIN_BINS];
+    uint64_t key[FAST_CAND];
+    int32_t id[FAST_CAND];
+    int counter, sink;
+  };
+  static_assert(sizeof(Dry) <= sizeof(s.lw) + sizeof(s.lp), "the dry run fits the list arrays");
+  Dry& d = *reinterpret_cast<Dry*>(s.lw);
+  const int lane = lane_id();
+  // Two tiles of a falling row, 16 down to 8.125 in steps of 1/8.
+  for (int h = 0; h < 2; ++h) d.row[lane + 32 * h] = T(16.f - 0.125f * float(lane + 32 * h));
+  if (lane < 2) d.tmax[lane] = W(16.f - 4.f * float(lane));
+  for (int b = lane; b < WIN_BINS; b += 32) d.counts[b] = b < 16 ? 1u : 0u;
+  if (lane == 0) d.counter = 0;
+  __syncwarp();
+  const int j = window_warp(d.counts, 2);
+  const SliceRef<T> src{d.row, 1, nullptr, 0, 64, 0};
+  const int m = gather_warp<T, W>(src, d.tmax, 0, 2, abs_bin(W(16)) - max(j, 0) - 8, d.key, d.id, &d.counter,
+                                  FAST_CAND);
+  __syncwarp();
+  ListIn in{d.key, d.id, min(m, FAST_CAND), 20, 16.0, 0.6, 0.01, 0.95, Address{1u, 2u, 3u, 4u}, 0, -1, nullptr};
+  const int sink = finish_warp<W>(in).sample;
+  in.verify = 1;
+  in.draft_id = d.id[3];
+  const ListOut o = finish_warp<W>(in);
+  if (lane == 0) d.sink = sink + o.accept + o.residual;
+}
+
 // MIN_BLOCKS: resident CTAs per SM the register allocation must allow (3 for
-// large streamed batches, else 2).
-template <int DT, int MIN_BLOCKS>
-__global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_constant__ Params p) {
+// large streamed batches, else 2). Blocks have THREADS row threads, plus a
+// warm-up warp with WARM (p.warm).
+template <int DT, int MIN_BLOCKS, bool WARM>
+__global__ void __launch_bounds__(THREADS + (WARM ? 32 : 0), MIN_BLOCKS) rows_kernel(const __grid_constant__ Params p) {
   using K = RowKernel<DT>;
   using R = typename K::R;
   using T = typename K::T;
@@ -393,7 +489,9 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_
   //    the preparation kernel: they are inputs, which it never writes.
   //    Resident rows copy the whole slice; streamed rows fill the TMA ring.
   bool lost = false;  // a bounded wait gave up: the row is not trusted
+  for (int i = threadIdx.x; i < ABS_BINS && int(threadIdx.x) < THREADS; i += THREADS) r.hist_abs[i] = 0;
   if (threadIdx.x == 0) {
+    s.n_cand = 0;  // rank 0's candidate counter, before any peer can push (the first cluster exchange)
     mbar_init(&s.bar, 1);
     for (int i = 0; i < MAX_RING_STAGES; ++i) mbar_init(&s.ring_bar[i], 1);
     mbar_init_fence();
@@ -414,6 +512,10 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_
     }
   }
   __syncthreads();
+  if (WARM && warp_id() >= WARPS) {  // the warm-up warp
+    warm_up<DT>(s);
+    return;
+  }
   if (r.sharded) {
     if (s.ctx.skip) return;  // the same on every rank of the cluster
     lost = s.timeout != 0;
@@ -447,7 +549,7 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_
       lost = true;
       break;
     }
-  lost = __syncthreads_or(lost);
+  lost = sync_rows_or(lost);
   ES_TRACE(p.workspace, p.rows, r.row, r.rank, 2);
   if (lost && threadIdx.x == 0) atomicAdd(&diagnostics(p.workspace, p.rows)->wait_timeouts, 1u);
 
@@ -532,7 +634,8 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) rows_kernel(const __grid_
 // programmatic stream serialization after the preparation kernel.
 template <int DT> cudaError_t launch_rows(const Params& p, int cluster, cudaStream_t stream) {
   const size_t smem = smem_bytes<DT>(p.slice_words, p.stream_rows);
-  auto kernel = p.min_blocks == 3 ? rows_kernel<DT, 3> : rows_kernel<DT, 2>;
+  auto kernel = p.min_blocks == 3 ? (p.warm ? rows_kernel<DT, 3, true> : rows_kernel<DT, 3, false>)
+                                  : (p.warm ? rows_kernel<DT, 2, true> : rows_kernel<DT, 2, false>);
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   if (cluster > 8) {
@@ -541,7 +644,7 @@ template <int DT> cudaError_t launch_rows(const Params& p, int cluster, cudaStre
   }
   cudaLaunchConfig_t config = {};
   config.gridDim = dim3(unsigned(cluster), unsigned(p.rows), 1);
-  config.blockDim = dim3(THREADS, 1, 1);
+  config.blockDim = dim3(p.warm ? THREADS + 32 : THREADS, 1, 1);
   config.dynamicSmemBytes = smem;
   config.stream = stream;
   cudaLaunchAttribute attrs[2];

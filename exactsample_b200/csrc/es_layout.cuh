@@ -80,6 +80,8 @@ struct Params {
   int32_t exact_draws;     // dispatch="reference": every draw scored in FP64, no lists
   int32_t stream_rows;     // 0: rows stay in shared memory; else the depth (2..4) of the TMA ring they stream through
   int32_t min_blocks;      // blocks per SM the row kernel's registers must allow (2, or 3 for large streamed batches)
+  int32_t fast;            // list rows of at most FAST_KEEP kept tokens may take the warp-level path (es_fast.cuh)
+  int32_t warm;            // the row kernel has a warm-up warp past its THREADS row threads
   Shards sh;
 };
 
@@ -161,7 +163,7 @@ __device__ __forceinline__ void trace_phase(uint8_t* ws, int64_t rows, int row, 
   if (threadIdx.x != 0) return;
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  reinterpret_cast<uint64_t*>(ws + 8 + rows * 1024)[(int64_t(row) * 16 + rank) * 16 + k] = t;
+  reinterpret_cast<uint64_t*>(ws + 8 + rows * 1024)[(int64_t(row) * 16 + rank) * 32 + k] = t;
 }
 #define ES_TRACE(ws, rows, row, rank, k) trace_phase(ws, rows, row, rank, k)
 #else

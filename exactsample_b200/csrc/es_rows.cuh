@@ -33,6 +33,7 @@
 //     over larger kept sets: a certified FP32 argmax of x + G with an FP64
 //     rescore of every token that could still win.
 #pragma once
+#include "es_fast.cuh"
 #include "es_prepare.cuh"
 
 namespace es {
@@ -43,10 +44,6 @@ template <> struct Types<ES_F64> { using T = double; using W = double; using Key
 template <> struct Types<ES_F16> { using T = __half; using W = float; using Key = uint32_t; };
 template <> struct Types<ES_BF16> { using T = __nv_bfloat16; using W = float; using Key = uint32_t; };
 
-__device__ __forceinline__ float widen(float v) { return v; }
-__device__ __forceinline__ double widen(double v) { return v; }
-__device__ __forceinline__ float widen(__half v) { return __half2float(v); }
-__device__ __forceinline__ float widen(__nv_bfloat16 v) { return __bfloat162float(v); }
 
 // Four consecutive values of a shared-memory slice.
 __device__ __forceinline__ void load4(const float* s, float v[4]) {
@@ -119,6 +116,7 @@ static __device__ __noinline__ bool weight_kept_fp64(double v, double maxv, doub
 template <class W> struct Stats {
   W vmax, qmax;  // largest valid target value; largest proposal value (full q)
   int32_t valid, bad, qvalid, qbad;
+  int32_t top_bin;  // abs_bin(vmax), -1 without a valid value
 };
 
 // A rank's share of an approximate kept-set mass (approx_mass): FP32 weights
@@ -178,6 +176,7 @@ template <class W> struct Smem {
     int32_t ints[16 * WINDOWS + 16];
   } peers;
   uint32_t peer_n[16];
+  uint32_t win[WIN_BINS];  // tile maxima of the whole row in the WIN_BINS absolute bins from the row's top bin down
   int32_t pushed[16];  // per-rank counts each rank writes into every rank's copy
   int32_t verdict;     // rank 0's decision on a top-p list, written into every rank's copy
   int32_t tiles[TILE_CAP];
@@ -195,10 +194,15 @@ template <class W> struct Smem {
     } cand;
     u128 mass[2][RADIX];
   } u;
-  // Rank 0's FP64 list: weights and probabilities in list order.
+  // Rank 0's FP64 list: weights and probabilities in list order. The
+  // warm-up warp uses them as scratch (it exits before the first cluster
+  // exchange, long before any list).
   double lw[LIST_MAX];
   double lp[LIST_MAX];
 };
+
+static_assert(sizeof(decltype(Smem<float>::u)) >= ABS_BINS * sizeof(uint32_t), "the tile histogram fits the candidate buffer");
+static_assert(sizeof(decltype(Smem<double>::u)) >= ABS_BINS * sizeof(uint32_t), "the tile histogram fits the candidate buffer");
 
 // Adds (v, 1) to bucket b of mass/count, aggregated over the warp's lanes that
 // share a bucket (one atomic per distinct bucket). Called by the whole warp;
@@ -234,6 +238,7 @@ template <int DT> struct Row {
   const Params& p;
   Smem<W>& s;
   uint32_t* mask_s;  // this rank's mask words (resident rows)
+  uint32_t* hist_abs;  // statistics pass: tile maxima per absolute bin (ABS_BINS, aliasing the candidate buffer)
   W* tmax;           // per 32-token tile of the slice: the largest valid value (-inf if none)
   T* slice;          // this rank's logits (resident rows) or the TMA ring (streamed rows)
   const T* tbase;    // the row in global memory (not sharded)
@@ -248,13 +253,15 @@ template <int DT> struct Row {
   // Row-level values, identical on every rank after the statistics merge.
   Stats<W> all;
   W maxv;
+  int top_bin;  // the row maximum's absolute bin (-1: no valid token)
   double temperature, top_p, min_p;
   float inv_t, ln_mp, mp_tol;
   bool slow_x, has_mask;
   Address addr;
 
   __device__ Row(const Params& p_, Smem<W>& s_, uint32_t* m, W* tm, T* sl)
-      : p(p_), s(s_), mask_s(m), tmax(tm), slice(sl), cluster(cg::this_cluster()) {
+      : p(p_), s(s_), mask_s(m), hist_abs(reinterpret_cast<uint32_t*>(&s_.u)), tmax(tm), slice(sl),
+        cluster(cg::this_cluster()) {
     rank = int(cluster.block_rank());
     ranks = int(cluster.num_blocks());
     row = blockIdx.y;
@@ -405,6 +412,7 @@ template <int DT> struct Row {
     m.bad = a.bad | b.bad;
     m.qvalid = a.qvalid + b.qvalid;
     m.qbad = a.qbad | b.qbad;
+    m.top_bin = a.top_bin > b.top_bin ? a.top_bin : b.top_bin;
     return m;
   }
   __device__ Stats<W> block_stats(Stats<W> v) {
@@ -414,13 +422,14 @@ template <int DT> struct Row {
       y.vmax = shfl_xor(v.vmax, o); y.qmax = shfl_xor(v.qmax, o);
       y.valid = shfl_xor(v.valid, o); y.bad = shfl_xor(v.bad, o); y.qvalid = shfl_xor(v.qvalid, o);
       y.qbad = shfl_xor(v.qbad, o);
+      y.top_bin = shfl_xor(v.top_bin, o);
       v = merge_stats(v, y);
     }
     if (lane_id() == 0) s.red.stats[warp_id()] = v;
-    __syncthreads();
+    sync_rows();
     Stats<W> m = s.red.stats[0];
     for (int w = 1; w < WARPS; ++w) m = merge_stats(m, s.red.stats[w]);
-    __syncthreads();
+    sync_rows();
     return m;
   }
   // Statistics accumulated over groups.
@@ -472,7 +481,10 @@ template <int DT> struct Row {
         const W other = shfl_xor(tile, o);
         tile = other > tile ? other : tile;
       }
-      if ((lane_id() & 7) == 0 && g < g_end) tmax[g >> 3] = tile;
+      if ((lane_id() & 7) == 0 && g < g_end) {
+        tmax[g >> 3] = tile;
+        if (tile > W(-INFINITY)) atomicAdd(&hist_abs[abs_bin(tile)], 1u);
+      }
     }
   }
   // Tiles (32 tokens) of this rank's slice; the last may be partial.
@@ -551,7 +563,7 @@ template <int DT> struct Row {
         const T* stage = slice + (c % stages) * (RING_CHUNK / sizeof(T)) - int64_t(c) * GPC * 4;
         stats_groups(c * GPC, min((c + 1) * GPC, ring_groups),
                      [&](int g, W v[4]) { load4(stage + 4 * g, v); }, a);
-        __syncthreads();  // every thread is done with this stage
+        sync_rows();  // every row thread is done with this stage
         if (threadIdx.x == 0 && c + stages < chunks) ring_issue(c + stages, c + stages);
       }
       ring_seq = chunks;
@@ -559,10 +571,17 @@ template <int DT> struct Row {
     } else {
       stats_groups(0, groups, [&](int g, W v[4]) { values(g, v); }, a);
     }
-    lost = __syncthreads_or(lost);
+    lost = sync_rows_or(lost);
     if (lost) a.bad = 1;  // a slice copy never arrived: the row is not trusted
-    const Stats<W> merged = block_stats(Stats<W>{a.best, W(-INFINITY), a.valid, a.bad, 0, 0});
+    const int own_top = a.best > W(-INFINITY) ? abs_bin(a.best) : -1;
+    const Stats<W> merged = block_stats(Stats<W>{a.best, W(-INFINITY), a.valid, a.bad, 0, 0, own_top});
+    // Publish the statistics and the WIN_BINS tile-maximum bins from this
+    // rank's top bin down (the histogram is complete: block_stats synced).
     if (threadIdx.x == 0) s.stats[parity()] = merged;
+    if (int(threadIdx.x) < WIN_BINS) {
+      const int b = merged.top_bin - int(threadIdx.x);
+      s.hist[parity()][threadIdx.x] = merged.top_bin >= 0 && b >= 0 ? hist_abs[b] : 0u;
+    }
     ES_TRACE(p.workspace, p.rows, row, rank, 8);
     exchange();
     ES_TRACE(p.workspace, p.rows, row, rank, 9);
@@ -571,7 +590,19 @@ template <int DT> struct Row {
     all = s.peers.stats[0];
     for (int r = 1; r < ranks; ++r) all = merge_stats(all, s.peers.stats[r]);
     maxv = all.vmax;
+    top_bin = all.top_bin;
     dense = !has_mask && all.valid == p.vocab;
+    // The row's tile maxima in the WIN_BINS bins from its top bin down: rank
+    // r published the bins from its own top bin (at most the row's) down.
+    if (p.fast && int(threadIdx.x) < WIN_BINS) {
+      uint32_t n = 0;
+      for (int r = 0; r < ranks; ++r) {
+        const int shift = top_bin - s.peers.stats[r].top_bin;  // >= 0
+        if (s.peers.stats[r].top_bin >= 0 && int(threadIdx.x) >= shift)
+          n += peer(s.hist[parity() ^ 1], r)[threadIdx.x - shift];
+      }
+      s.win[threadIdx.x] = n;
+    }
     __syncthreads();
     return !lost;
   }
