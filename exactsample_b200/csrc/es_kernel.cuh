@@ -302,11 +302,34 @@ template <int DT> struct RowKernel {
                    : SliceRef<T>{r.tbase + int64_t(r.lo) * p.t_s1, p.t_s1,
                                  r.has_mask ? p.mask + int64_t(r.row) * p.m_s0 + int64_t(r.lo >> 5) * p.m_s1 : nullptr,
                                  p.m_s1, r.hi - r.lo, r.lo};
-    const int nt = r.tile_count();
-    const int per = (nt + WARPS - 1) / WARPS;
-    const int t0 = min(nt, warp_id() * per), t1 = min(nt, t0 + per);
-    int mine = gather_warp<T, W>(src, r.tmax, t0, t1, bin, r.peer(s.u.cand.key, 0), r.peer(s.u.cand.id, 0),
-                                 r.peer(&s.n_cand, 0), CAP);
+    // Streamed rows: when every one of this rank's window tiles is in its
+    // warps' caches (their count against the rank's own histogram), the
+    // gather reads shared memory only.
+    bool cached = false;
+    if (r.direct) {
+      auto& tc = r.cache();
+      const int w = warp_id(), lane = lane_id();
+      const int in_cache = __popc(__ballot_sync(0xffffffffu, lane < tc.count[w] && abs_bin(tc.tmax[w][lane]) >= bin));
+      const int own_top = s.in_stats[r.rank].top_bin;
+      int window_tiles = 0;
+      for (int k = lane; k <= own_top - bin && k < WIN_BINS; k += 32) window_tiles += s.in_win[r.rank][k];
+      window_tiles = __reduce_add_sync(0xffffffffu, uint32_t(window_tiles));
+      const int have = block_all(lane == 0 ? in_cache : 0, [](int x, int y) { return x + y; }, s.red.ints);
+      cached = have == window_tiles;  // every warp computed window_tiles alike
+    }
+    int mine;
+    if (cached) {
+      auto& tc = r.cache();
+      const int w = warp_id();
+      mine = gather_cached_warp<W>(&tc.val[w][0][0], tc.tmax[w], tc.tile[w], tc.count[w], r.lo, bin,
+                                   r.peer(s.u.cand.key, 0), r.peer(s.u.cand.id, 0), r.peer(&s.n_cand, 0), CAP);
+    } else {
+      const int nt = r.tile_count();
+      const int per = (nt + WARPS - 1) / WARPS;
+      const int t0 = min(nt, warp_id() * per), t1 = min(nt, t0 + per);
+      mine = gather_warp<T, W>(src, r.tmax, t0, t1, bin, r.peer(s.u.cand.key, 0), r.peer(s.u.cand.id, 0),
+                               r.peer(&s.n_cand, 0), CAP);
+    }
     mine = block_all(lane_id() == 0 ? mine : 0, [](int x, int y) { return x + y; }, s.red.ints);
     if (int(threadIdx.x) < r.ranks) r.peer(s.pushed, threadIdx.x)[r.rank] = mine;
     ES_TRACE(p.workspace, p.rows, r.row, r.rank, 14);
@@ -439,6 +462,7 @@ template <int DT> __device__ void warm_up(Smem<typename Types<DT>::W>& s) {
   using W = typename Types<DT>::W;
   struct Dry {
     T row[64];
+    W cval[64];
     W tmax[2];
     uint32_t counts[WIN_BINS];
     uint64_t key[FAST_CAND];
@@ -449,15 +473,23 @@ template <int DT> __device__ void warm_up(Smem<typename Types<DT>::W>& s) {
   Dry& d = *reinterpret_cast<Dry*>(s.lw);
   const int lane = lane_id();
   // Two tiles of a falling row, 16 down to 8.125 in steps of 1/8.
-  for (int h = 0; h < 2; ++h) d.row[lane + 32 * h] = T(16.f - 0.125f * float(lane + 32 * h));
+  for (int h = 0; h < 2; ++h) {
+    d.row[lane + 32 * h] = T(16.f - 0.125f * float(lane + 32 * h));
+    d.cval[lane + 32 * h] = W(16.f - 0.125f * float(lane + 32 * h));
+  }
   if (lane < 2) d.tmax[lane] = W(16.f - 4.f * float(lane));
   for (int b = lane; b < WIN_BINS; b += 32) d.counts[b] = b < 16 ? 1u : 0u;
   if (lane == 0) d.counter = 0;
   __syncwarp();
   const int j = window_warp(d.counts, 2);
   const SliceRef<T> src{d.row, 1, nullptr, 0, 64, 0};
-  const int m = gather_warp<T, W>(src, d.tmax, 0, 2, abs_bin(W(16)) - max(j, 0) - 8, d.key, d.id, &d.counter,
-                                  FAST_CAND);
+  const int bin = abs_bin(W(16)) - max(j, 0) - 8;
+  const int tiles[2] = {0, 1};
+  int m = gather_cached_warp<W>(d.cval, d.tmax, tiles, 2, 0, bin, d.key, d.id, &d.counter, FAST_CAND);
+  __syncwarp();
+  if (lane == 0) d.counter = 0;
+  __syncwarp();
+  m = min(m, gather_warp<T, W>(src, d.tmax, 0, 2, bin, d.key, d.id, &d.counter, FAST_CAND));
   __syncwarp();
   ListIn in{d.key, d.id, min(m, FAST_CAND), 20, 16.0, 0.6, 0.01, 0.95, Address{1u, 2u, 3u, 4u}, 0, -1, nullptr};
   const int sink = finish_warp<W>(in).sample;
@@ -524,7 +556,7 @@ __global__ void __launch_bounds__(THREADS + (WARM ? 32 : 0), MIN_BLOCKS) rows_ke
   if (stream) {
     if (threadIdx.x == 0) {
       mbar_arrive_expect_tx(&s.bar, 0);
-      if (p.vector_load)
+      if (p.vector_load && !r.direct)  // direct rows read the slice themselves (the ring holds their tile cache)
         for (int c = 0; c < min(p.stream_rows, r.ring_chunks()); ++c) r.ring_issue(c, c);
     }
   } else if (p.vector_load) {
@@ -558,17 +590,9 @@ __global__ void __launch_bounds__(THREADS + (WARM ? 32 : 0), MIN_BLOCKS) rows_ke
   ES_TRACE(p.workspace, p.rows, r.row, r.rank, 3);
 
   // 4. The preparation kernel's statuses and counters; the row's request and
-  //    parameters (the same on every rank), gathered by it.
-  wait_for_prerequisite_grid();
+  //    parameters (the same on every rank), gathered by it and loaded by
+  //    the statistics pass before its exchange.
   ES_TRACE(p.workspace, p.rows, r.row, r.rank, 1);
-  if (threadIdx.x == 0) {
-    if (*malformed_flag(p.workspace) != 0) {
-      s.ctx.skip = 1;
-    } else {
-      s.ctx = row_contexts(p.workspace, p.rows)[r.row];
-    }
-  }
-  __syncthreads();
   if (s.ctx.skip) {  // the same decision on every rank; every copy has landed
     r.cluster.sync();  // no rank leaves while a peer may still read its statistics slot
     return;

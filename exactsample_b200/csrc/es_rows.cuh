@@ -177,6 +177,12 @@ template <class W> struct Smem {
   } peers;
   uint32_t peer_n[16];
   uint32_t win[WIN_BINS];  // tile maxima of the whole row in the WIN_BINS absolute bins from the row's top bin down
+  // The statistics exchange's inbox: every rank stores its statistics and
+  // tile-maximum bins (from its own top bin down) into every rank's slot
+  // before the exchange, so that afterwards each rank reads only its own
+  // shared memory.
+  Stats<W> in_stats[16];
+  uint16_t in_win[16][WIN_BINS];
   int32_t pushed[16];  // per-rank counts each rank writes into every rank's copy
   int32_t verdict;     // rank 0's decision on a top-p list, written into every rank's copy
   int32_t tiles[TILE_CAP];
@@ -243,6 +249,7 @@ template <int DT> struct Row {
   T* slice;          // this rank's logits (resident rows) or the TMA ring (streamed rows)
   const T* tbase;    // the row in global memory (not sharded)
   bool resident, vec, sharded;
+  bool direct;  // streamed rows read straight from global memory by the statistics pass (hot tiles cached)
   bool dense;  // after the statistics: no mask and every token of the row valid
   cg::cluster_group cluster;
   int rank, ranks, row, lo, hi, groups;
@@ -275,6 +282,7 @@ template <int DT> struct Row {
     resident = !p.stream_rows;
     vec = p.vector_load != 0;
     sharded = p.sh.count > 1;
+    direct = !resident && vec && !sharded;
     dense = false;
     tbase = static_cast<const T*>(p.target) + int64_t(row) * p.t_s0;
   }
@@ -541,6 +549,153 @@ template <int DT> struct Row {
     bulk_columns(reinterpret_cast<uint8_t*>(slice) + stage * RING_CHUNK, lo + int(off / sizeof(T)),
                  int(len / sizeof(T)), bar);
   }
+  // ---- streamed rows read directly, with a cache of hot tiles ----
+  // Each warp keeps up to CACHE_SLOTS of its tiles whose maximum was within
+  // CACHE_DEPTH logits of the warp's running maximum when it read them, in
+  // the TMA ring's shared memory (unused until a later whole-row pass, which
+  // only rows off the warp-level list path make). The list gather then takes
+  // the window's tiles from here instead of from L2 when all of them are
+  // cached (es_kernel.cuh fast_list); otherwise it reads them again.
+  static constexpr int CACHE_SLOTS = sizeof(W) == 8 ? 14 : 28;
+  static constexpr float CACHE_DEPTH = 12.f;
+  struct TileCache {
+    W val[WARPS][CACHE_SLOTS][32];
+    W tmax[WARPS][CACHE_SLOTS];
+    int32_t tile[WARPS][CACHE_SLOTS];
+    int32_t count[WARPS];
+  };
+  static_assert(sizeof(TileCache) <= 2 * RING_CHUNK, "the tile cache fits the smallest ring");
+  static_assert(CACHE_SLOTS <= 32, "one lane per cache slot");
+  __device__ __forceinline__ TileCache& cache() const { return *reinterpret_cast<TileCache*>(slice); }
+
+  // The warp's largest value (warp-uniform), by reductions over order keys.
+  __device__ __forceinline__ static W warp_max(W v) {
+    constexpr unsigned ALL = 0xffffffffu;
+    if constexpr (sizeof(W) == 8) {
+      const uint64_t k = order_key(v);
+      const uint32_t hi_ = __reduce_max_sync(ALL, uint32_t(k >> 32));
+      const uint32_t lo_ = __reduce_max_sync(ALL, uint32_t(k >> 32) == hi_ ? uint32_t(k) : 0u);
+      return key_value((uint64_t(hi_) << 32) | lo_);
+    } else {
+      return key_value(__reduce_max_sync(ALL, order_key(v)));
+    }
+  }
+  // Drops the warp's cached tiles whose maximum is below thr (order kept);
+  // returns the new count. Lane s looks after slot s's column of values.
+  __device__ int cache_compact(int count, W thr) {
+    TileCache& tc = cache();
+    const int w = warp_id(), lane = lane_id();
+    __syncwarp();  // the slots' maxima, written by their tiles' leader lanes
+    const bool keep = lane < count && tc.tmax[w][lane] >= thr;
+    const unsigned kept = __ballot_sync(0xffffffffu, keep);
+    for (unsigned rest = kept; rest; rest &= rest - 1) {
+      const int src = __ffs(rest) - 1, dst = __popc(kept & ((1u << src) - 1u));
+      if (dst == src) continue;
+      tc.val[w][dst][lane] = tc.val[w][src][lane];
+      if (lane == 0) {
+        tc.tmax[w][dst] = tc.tmax[w][src];
+        tc.tile[w][dst] = tc.tile[w][src];
+      }
+    }
+    __syncwarp();
+    return __popc(kept);
+  }
+  // The statistics of the slice's whole tiles, read from global memory with
+  // U groups per lane in flight: warp w takes a contiguous share of the
+  // tiles. Per group as stats_groups; each tile's maximum goes to tmax and
+  // to the absolute histogram, and tiles near the warp's running maximum
+  // into the warp's cache.
+  __device__ void stats_direct(Acc& a) {
+    constexpr int U = sizeof(T) == 2 ? 8 : sizeof(T) == 4 ? 4 : 2;
+    constexpr unsigned ALL = 0xffffffffu;
+    TileCache& tc = cache();
+    const int w = warp_id(), lane = lane_id();
+    const int full = (hi - lo) / 32;
+    const int per = (full + WARPS - 1) / WARPS;
+    const int t0 = min(full, w * per), t1 = min(full, t0 + per);
+    const int g_end = 8 * t1;
+    const T* base = tbase + lo;  // vec rows: unit column stride
+    int count = 0;
+    for (int g0 = 8 * t0; g0 < g_end; g0 += 32 * U) {
+      W v[U][4];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int g = g0 + 32 * u + lane;
+        if (g < g_end) {
+          load4_global(base + 4 * g, v[u]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) v[u][j] = W(-INFINITY);
+        }
+      }
+      W tile[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int g = g0 + 32 * u + lane;
+        W t = W(-INFINITY);
+        if (g < g_end) {
+          if (!has_mask) {
+            const W q = (v[u][0] * W(0.25) + v[u][1] * W(0.25)) + (v[u][2] * W(0.25) + v[u][3] * W(0.25));
+            a.bad |= !(q < W(INFINITY));
+            int n = 4;
+            if (q == W(-INFINITY))
+              n = int(v[u][0] > W(-INFINITY)) + int(v[u][1] > W(-INFINITY)) + int(v[u][2] > W(-INFINITY)) +
+                  int(v[u][3] > W(-INFINITY));
+            a.valid += n;
+            const W m01 = v[u][0] > v[u][1] ? v[u][0] : v[u][1], m23 = v[u][2] > v[u][3] ? v[u][2] : v[u][3];
+            t = m01 > m23 ? m01 : m23;
+          } else {
+            const unsigned bits = group_bits(g);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              a.bad |= !(v[u][j] < W(INFINITY)) & (v[u][j] != W(-INFINITY));  // NaN or +inf
+              const bool ok = ((bits >> j) & 1u) && v[u][j] > W(-INFINITY);
+              a.valid += ok;
+              if (!ok) v[u][j] = W(-INFINITY);  // the cache holds valid tokens only
+              if (ok && v[u][j] > t) t = v[u][j];
+            }
+          }
+          if (t > a.best) a.best = t;
+        }
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+          const W other = shfl_xor(t, o);
+          t = other > t ? other : t;
+        }
+        tile[u] = t;
+        if ((lane & 7) == 0 && g < g_end) {
+          tmax[g >> 3] = t;
+          if (t > W(-INFINITY)) atomicAdd(&hist_abs[abs_bin(t)], 1u);
+        }
+      }
+      // Cache the tiles within CACHE_DEPTH of the warp's running maximum.
+      const W thr = warp_max(a.best) - W(CACHE_DEPTH);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int g = g0 + 32 * u + lane;
+        const unsigned leads =
+            __ballot_sync(ALL, (lane & 7) == 0 && g < g_end && tile[u] > W(-INFINITY) && tile[u] >= thr);
+        if (!leads) continue;
+        const int c = __popc(leads);
+        if (count + c > CACHE_SLOTS) count = cache_compact(count, thr);
+        const int room = CACHE_SLOTS - count;
+        const unsigned lead = 1u << (lane & ~7);
+        const int k = __popc(leads & (lead - 1u));
+        if ((leads & lead) && k < room) {
+          const int slot = count + k;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tc.val[w][slot][4 * (lane & 7) + j] = v[u][j];
+          if ((lane & 7) == 0) {
+            tc.tmax[w][slot] = tile[u];
+            tc.tile[w][slot] = g >> 3;
+          }
+        }
+        count += min(c, room);
+      }
+    }
+    if (lane == 0) tc.count[w] = count;
+  }
+
   // The statistics pass over the whole slice: from shared memory (resident),
   // through the TMA ring (streamed, 16-byte aligned rows), or from global
   // memory; then the cluster merge. Returns false if a copy never arrived.
@@ -549,6 +704,9 @@ template <int DT> struct Row {
     bool lost = timed_out;
     if (resident) {
       stats_groups(0, groups, [&](int g, W v[4]) { load4(slice + 4 * g, v); }, a);
+    } else if (direct) {
+      stats_direct(a);
+      stats_groups(8 * ((hi - lo) / 32), groups, [&](int g, W v[4]) { values(g, v); }, a);  // a last partial tile
     } else if (vec) {
       constexpr int GPC = int(RING_CHUNK / (4 * sizeof(T)));  // groups per chunk
       const int ring_groups = int(ring_bytes() / (4 * sizeof(T))) & ~7;  // whole tiles
@@ -575,31 +733,37 @@ template <int DT> struct Row {
     if (lost) a.bad = 1;  // a slice copy never arrived: the row is not trusted
     const int own_top = a.best > W(-INFINITY) ? abs_bin(a.best) : -1;
     const Stats<W> merged = block_stats(Stats<W>{a.best, W(-INFINITY), a.valid, a.bad, 0, 0, own_top});
-    // Publish the statistics and the WIN_BINS tile-maximum bins from this
-    // rank's top bin down (the histogram is complete: block_stats synced).
-    if (threadIdx.x == 0) s.stats[parity()] = merged;
+    // Store the statistics and the WIN_BINS tile-maximum bins from this
+    // rank's top bin down into every rank's inbox (the histogram is
+    // complete: block_stats synced); the exchange orders the stores.
+    if (int(threadIdx.x) < ranks) *peer(&s.in_stats[rank], threadIdx.x) = merged;
     if (int(threadIdx.x) < WIN_BINS) {
       const int b = merged.top_bin - int(threadIdx.x);
-      s.hist[parity()][threadIdx.x] = merged.top_bin >= 0 && b >= 0 ? hist_abs[b] : 0u;
+      const uint16_t n = uint16_t(merged.top_bin >= 0 && b >= 0 ? min(hist_abs[b], 65535u) : 0u);
+      for (int r = 0; r < ranks; ++r) peer(s.in_win[rank], r)[threadIdx.x] = n;
+    }
+    // The preparation kernel's outputs: its grid is long done by now, so the
+    // context load overlaps the exchange.
+    wait_for_prerequisite_grid();
+    if (threadIdx.x == 0) {
+      if (*malformed_flag(p.workspace) != 0) s.ctx.skip = 1;
+      else s.ctx = row_contexts(p.workspace, p.rows)[row];
     }
     ES_TRACE(p.workspace, p.rows, row, rank, 8);
     exchange();
     ES_TRACE(p.workspace, p.rows, row, rank, 9);
-    if (int(threadIdx.x) < ranks) s.peers.stats[threadIdx.x] = *peer(&s.stats[parity() ^ 1], threadIdx.x);
-    __syncthreads();
-    all = s.peers.stats[0];
-    for (int r = 1; r < ranks; ++r) all = merge_stats(all, s.peers.stats[r]);
+    all = s.in_stats[0];
+    for (int r = 1; r < ranks; ++r) all = merge_stats(all, s.in_stats[r]);
     maxv = all.vmax;
     top_bin = all.top_bin;
     dense = !has_mask && all.valid == p.vocab;
     // The row's tile maxima in the WIN_BINS bins from its top bin down: rank
-    // r published the bins from its own top bin (at most the row's) down.
+    // r sent the bins from its own top bin (at most the row's) down.
     if (p.fast && int(threadIdx.x) < WIN_BINS) {
       uint32_t n = 0;
       for (int r = 0; r < ranks; ++r) {
-        const int shift = top_bin - s.peers.stats[r].top_bin;  // >= 0
-        if (s.peers.stats[r].top_bin >= 0 && int(threadIdx.x) >= shift)
-          n += peer(s.hist[parity() ^ 1], r)[threadIdx.x - shift];
+        const int shift = top_bin - s.in_stats[r].top_bin;  // >= 0
+        if (s.in_stats[r].top_bin >= 0 && int(threadIdx.x) >= shift) n += s.in_win[r][threadIdx.x - shift];
       }
       s.win[threadIdx.x] = n;
     }
