@@ -309,7 +309,8 @@ template <int DT> struct RowKernel {
     if (r.direct) {
       auto& tc = r.cache();
       const int w = warp_id(), lane = lane_id();
-      const int in_cache = __popc(__ballot_sync(0xffffffffu, lane < tc.count[w] && abs_bin(tc.tmax[w][lane]) >= bin));
+      const int in_cache =
+          __popc(__ballot_sync(0xffffffffu, lane < tc.count[w] && abs_bin(tc.warp[w].tmax[lane]) >= bin));
       const int own_top = s.in_stats[r.rank].top_bin;
       int window_tiles = 0;
       for (int k = lane; k <= own_top - bin && k < WIN_BINS; k += 32) window_tiles += s.in_win[r.rank][k];
@@ -321,7 +322,7 @@ template <int DT> struct RowKernel {
     if (cached) {
       auto& tc = r.cache();
       const int w = warp_id();
-      mine = gather_cached_warp<W>(&tc.val[w][0][0], tc.tmax[w], tc.tile[w], tc.count[w], r.lo, bin,
+      mine = gather_cached_warp<W>(&tc.warp[w].val[0][0], tc.warp[w].tmax, tc.warp[w].tile, tc.count[w], r.lo, bin,
                                    r.peer(s.u.cand.key, 0), r.peer(s.u.cand.id, 0), r.peer(&s.n_cand, 0), CAP);
     } else {
       const int nt = r.tile_count();

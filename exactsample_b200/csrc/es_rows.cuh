@@ -45,40 +45,6 @@ template <> struct Types<ES_F16> { using T = __half; using W = float; using Key 
 template <> struct Types<ES_BF16> { using T = __nv_bfloat16; using W = float; using Key = uint32_t; };
 
 
-// Four consecutive values of a shared-memory slice.
-__device__ __forceinline__ void load4(const float* s, float v[4]) {
-  const float4 x = *reinterpret_cast<const float4*>(s);
-  v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
-}
-__device__ __forceinline__ void load4(const double* s, double v[4]) {
-  const double2 x = reinterpret_cast<const double2*>(s)[0], y = reinterpret_cast<const double2*>(s)[1];
-  v[0] = x.x; v[1] = x.y; v[2] = y.x; v[3] = y.y;
-}
-__device__ __forceinline__ void load4(const __nv_bfloat16* s, float v[4]) {
-  const uint2 x = *reinterpret_cast<const uint2*>(s);
-  v[0] = __uint_as_float(x.x << 16); v[1] = __uint_as_float(x.x & 0xffff0000u);
-  v[2] = __uint_as_float(x.y << 16); v[3] = __uint_as_float(x.y & 0xffff0000u);
-}
-__device__ __forceinline__ void load4(const __half* s, float v[4]) {
-  const uint2 x = *reinterpret_cast<const uint2*>(s);
-  v[0] = __half2float(__ushort_as_half(uint16_t(x.x))); v[1] = __half2float(__ushort_as_half(uint16_t(x.x >> 16)));
-  v[2] = __half2float(__ushort_as_half(uint16_t(x.y))); v[3] = __half2float(__ushort_as_half(uint16_t(x.y >> 16)));
-}
-
-// Four consecutive values from global memory (16-byte aligned rows).
-__device__ __forceinline__ void load4_global(const float* g, float v[4]) {
-  const float4 x = __ldg(reinterpret_cast<const float4*>(g));
-  v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
-}
-__device__ __forceinline__ void load4_global(const double* g, double v[4]) {
-  const double2 x = __ldg(reinterpret_cast<const double2*>(g)), y = __ldg(reinterpret_cast<const double2*>(g) + 1);
-  v[0] = x.x; v[1] = x.y; v[2] = y.x; v[3] = y.y;
-}
-template <class H> __device__ __forceinline__ void load4_global(const H* g, float v[4]) {
-  const uint2 x = __ldg(reinterpret_cast<const uint2*>(g));
-  load4(reinterpret_cast<const H*>(&x), v);
-}
-
 // An exact cut of the order (value desc, token ID asc): keeps the tokens at or
 // before (key, id). `on == 0` keeps everything.
 template <class Key> struct Cut {
@@ -559,141 +525,28 @@ template <int DT> struct Row {
   static constexpr int CACHE_SLOTS = sizeof(W) == 8 ? 14 : 28;
   static constexpr float CACHE_DEPTH = 12.f;
   struct TileCache {
-    W val[WARPS][CACHE_SLOTS][32];
-    W tmax[WARPS][CACHE_SLOTS];
-    int32_t tile[WARPS][CACHE_SLOTS];
+    WarpCache<W, CACHE_SLOTS> warp[WARPS];
     int32_t count[WARPS];
   };
   static_assert(sizeof(TileCache) <= 2 * RING_CHUNK, "the tile cache fits the smallest ring");
   static_assert(CACHE_SLOTS <= 32, "one lane per cache slot");
   __device__ __forceinline__ TileCache& cache() const { return *reinterpret_cast<TileCache*>(slice); }
 
-  // The warp's largest value (warp-uniform), by reductions over order keys.
-  __device__ __forceinline__ static W warp_max(W v) {
-    constexpr unsigned ALL = 0xffffffffu;
-    if constexpr (sizeof(W) == 8) {
-      const uint64_t k = order_key(v);
-      const uint32_t hi_ = __reduce_max_sync(ALL, uint32_t(k >> 32));
-      const uint32_t lo_ = __reduce_max_sync(ALL, uint32_t(k >> 32) == hi_ ? uint32_t(k) : 0u);
-      return key_value((uint64_t(hi_) << 32) | lo_);
-    } else {
-      return key_value(__reduce_max_sync(ALL, order_key(v)));
-    }
-  }
-  // Drops the warp's cached tiles whose maximum is below thr (order kept);
-  // returns the new count. Lane s looks after slot s's column of values.
-  __device__ int cache_compact(int count, W thr) {
-    TileCache& tc = cache();
-    const int w = warp_id(), lane = lane_id();
-    __syncwarp();  // the slots' maxima, written by their tiles' leader lanes
-    const bool keep = lane < count && tc.tmax[w][lane] >= thr;
-    const unsigned kept = __ballot_sync(0xffffffffu, keep);
-    for (unsigned rest = kept; rest; rest &= rest - 1) {
-      const int src = __ffs(rest) - 1, dst = __popc(kept & ((1u << src) - 1u));
-      if (dst == src) continue;
-      tc.val[w][dst][lane] = tc.val[w][src][lane];
-      if (lane == 0) {
-        tc.tmax[w][dst] = tc.tmax[w][src];
-        tc.tile[w][dst] = tc.tile[w][src];
-      }
-    }
-    __syncwarp();
-    return __popc(kept);
-  }
-  // The statistics of the slice's whole tiles, read from global memory with
-  // U groups per lane in flight: warp w takes a contiguous share of the
-  // tiles. Per group as stats_groups; each tile's maximum goes to tmax and
-  // to the absolute histogram, and tiles near the warp's running maximum
-  // into the warp's cache.
+  // The statistics of the slice's whole tiles, read from global memory by
+  // stream_tiles_warp (es_fast.cuh): warp w takes a contiguous share of the
+  // tiles and fills its own cache.
   __device__ void stats_direct(Acc& a) {
-    constexpr int U = sizeof(T) == 2 ? 8 : sizeof(T) == 4 ? 4 : 2;
-    constexpr unsigned ALL = 0xffffffffu;
-    TileCache& tc = cache();
-    const int w = warp_id(), lane = lane_id();
+    const int w = warp_id();
     const int full = (hi - lo) / 32;
     const int per = (full + WARPS - 1) / WARPS;
     const int t0 = min(full, w * per), t1 = min(full, t0 + per);
-    const int g_end = 8 * t1;
-    const T* base = tbase + lo;  // vec rows: unit column stride
-    int count = 0;
-    for (int g0 = 8 * t0; g0 < g_end; g0 += 32 * U) {
-      W v[U][4];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int g = g0 + 32 * u + lane;
-        if (g < g_end) {
-          load4_global(base + 4 * g, v[u]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) v[u][j] = W(-INFINITY);
-        }
-      }
-      W tile[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int g = g0 + 32 * u + lane;
-        W t = W(-INFINITY);
-        if (g < g_end) {
-          if (!has_mask) {
-            const W q = (v[u][0] * W(0.25) + v[u][1] * W(0.25)) + (v[u][2] * W(0.25) + v[u][3] * W(0.25));
-            a.bad |= !(q < W(INFINITY));
-            int n = 4;
-            if (q == W(-INFINITY))
-              n = int(v[u][0] > W(-INFINITY)) + int(v[u][1] > W(-INFINITY)) + int(v[u][2] > W(-INFINITY)) +
-                  int(v[u][3] > W(-INFINITY));
-            a.valid += n;
-            const W m01 = v[u][0] > v[u][1] ? v[u][0] : v[u][1], m23 = v[u][2] > v[u][3] ? v[u][2] : v[u][3];
-            t = m01 > m23 ? m01 : m23;
-          } else {
-            const unsigned bits = group_bits(g);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              a.bad |= !(v[u][j] < W(INFINITY)) & (v[u][j] != W(-INFINITY));  // NaN or +inf
-              const bool ok = ((bits >> j) & 1u) && v[u][j] > W(-INFINITY);
-              a.valid += ok;
-              if (!ok) v[u][j] = W(-INFINITY);  // the cache holds valid tokens only
-              if (ok && v[u][j] > t) t = v[u][j];
-            }
-          }
-          if (t > a.best) a.best = t;
-        }
-#pragma unroll
-        for (int o = 1; o < 8; o <<= 1) {
-          const W other = shfl_xor(t, o);
-          t = other > t ? other : t;
-        }
-        tile[u] = t;
-        if ((lane & 7) == 0 && g < g_end) {
-          tmax[g >> 3] = t;
-          if (t > W(-INFINITY)) atomicAdd(&hist_abs[abs_bin(t)], 1u);
-        }
-      }
-      // Cache the tiles within CACHE_DEPTH of the warp's running maximum.
-      const W thr = warp_max(a.best) - W(CACHE_DEPTH);
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int g = g0 + 32 * u + lane;
-        const unsigned leads =
-            __ballot_sync(ALL, (lane & 7) == 0 && g < g_end && tile[u] > W(-INFINITY) && tile[u] >= thr);
-        if (!leads) continue;
-        const int c = __popc(leads);
-        if (count + c > CACHE_SLOTS) count = cache_compact(count, thr);
-        const int room = CACHE_SLOTS - count;
-        const unsigned lead = 1u << (lane & ~7);
-        const int k = __popc(leads & (lead - 1u));
-        if ((leads & lead) && k < room) {
-          const int slot = count + k;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) tc.val[w][slot][4 * (lane & 7) + j] = v[u][j];
-          if ((lane & 7) == 0) {
-            tc.tmax[w][slot] = tile[u];
-            tc.tile[w][slot] = g >> 3;
-          }
-        }
-        count += min(c, room);
-      }
-    }
-    if (lane == 0) tc.count[w] = count;
+    const StreamIn<T, W, CACHE_SLOTS> in{
+        tbase + lo, has_mask ? p.mask + int64_t(row) * p.m_s0 + int64_t(lo >> 5) * p.m_s1 : nullptr, p.m_s1,
+        8 * t0, 8 * t1, tmax, hist_abs, &cache().warp[w], &cache().count[w], W(CACHE_DEPTH)};
+    const StreamOut<W> o = stream_tiles_warp<T, W, CACHE_SLOTS>(in);
+    if (o.best > a.best) a.best = o.best;
+    a.valid += o.valid;
+    a.bad |= o.bad;
   }
 
   // The statistics pass over the whole slice: from shared memory (resident),
