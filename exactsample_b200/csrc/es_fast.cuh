@@ -273,157 +273,6 @@ template <class W, int SLOTS> struct WarpCache {
   int32_t tile[SLOTS];
 };
 
-// What stream_tiles_warp reads and writes.
-template <class T, class W, int SLOTS> struct StreamIn {
-  const T* values;      // slice element 0 in global memory (unit stride, 16-byte aligned)
-  const int32_t* mask;  // the slice's first mask word (NULL: no mask), word stride mstride
-  int64_t mstride;
-  int g0, g1;           // this warp's groups, whole tiles: [g0, g1), multiples of 8
-  W* tmax;              // per tile of the slice: the largest valid value
-  uint32_t* hist;       // tiles per absolute bin of their maximum (ABS_BINS)
-  WarpCache<W, SLOTS>* cache;
-  int32_t* cache_count;
-  W depth;              // tiles within this of the warp's running maximum are cached
-};
-template <class W> struct StreamOut {
-  W best;  // this lane's largest valid value
-  int valid, bad;
-};
-
-// The statistics of whole tiles read straight from global memory, U groups
-// (of four tokens) per lane in flight, by one warp: NaN / +inf anywhere
-// (even masked), the valid count and maximum, each tile's maximum (to tmax
-// and to the absolute histogram), and a copy of each tile whose maximum is
-// within `depth` of the warp's running maximum into the warp's cache (when
-// it is full, tiles below the current threshold are dropped first; a tile
-// that still finds no room is not cached). Out of line, so that the loop
-// has the register file to itself. A whole unmasked group uses the
-// quarter-sum test of Row::stats_groups (es_rows.cuh).
-template <class T, class W, int SLOTS>
-__device__ __noinline__ StreamOut<W> stream_tiles_warp(const StreamIn<T, W, SLOTS>& in) {
-  constexpr int U = sizeof(T) == 2 ? 8 : sizeof(T) == 4 ? 4 : 2;
-  constexpr unsigned ALL = 0xffffffffu;
-  const int lane = lane_id();
-  const T* values = in.values;
-  const int32_t* mask = in.mask;
-  const int64_t mstride = in.mstride;
-  const int g_end = in.g1;
-  W* tmax = in.tmax;
-  uint32_t* hist = in.hist;
-  WarpCache<W, SLOTS>& c = *in.cache;
-  const W depth = in.depth;
-  StreamOut<W> a{W(-INFINITY), 0, 0};
-  int count = 0;
-  for (int g0 = in.g0; g0 < g_end; g0 += 32 * U) {
-    W v[U][4];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int g = g0 + 32 * u + lane;
-      if (g < g_end) {
-        load4_global(values + 4 * g, v[u]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) v[u][j] = W(-INFINITY);
-      }
-    }
-    W tile[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int g = g0 + 32 * u + lane;
-      W t = W(-INFINITY);
-      if (g < g_end) {
-        if (mask == nullptr) {
-          const W q = (v[u][0] * W(0.25) + v[u][1] * W(0.25)) + (v[u][2] * W(0.25) + v[u][3] * W(0.25));
-          a.bad |= !(q < W(INFINITY));
-          int n = 4;
-          if (q == W(-INFINITY))
-            n = int(v[u][0] > W(-INFINITY)) + int(v[u][1] > W(-INFINITY)) + int(v[u][2] > W(-INFINITY)) +
-                int(v[u][3] > W(-INFINITY));
-          a.valid += n;
-          const W m01 = v[u][0] > v[u][1] ? v[u][0] : v[u][1], m23 = v[u][2] > v[u][3] ? v[u][2] : v[u][3];
-          t = m01 > m23 ? m01 : m23;
-        } else {
-          const uint32_t word = uint32_t(__ldg(mask + int64_t(g >> 3) * mstride));
-          const unsigned bits = (word >> ((4 * g) & 31)) & 0xfu;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            a.bad |= !(v[u][j] < W(INFINITY)) & (v[u][j] != W(-INFINITY));  // NaN or +inf
-            const bool ok = ((bits >> j) & 1u) && v[u][j] > W(-INFINITY);
-            a.valid += ok;
-            if (!ok) v[u][j] = W(-INFINITY);  // the cache holds valid tokens only
-            if (ok && v[u][j] > t) t = v[u][j];
-          }
-        }
-        if (t > a.best) a.best = t;
-      }
-#pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
-        const W other = __shfl_xor_sync(ALL, t, o);
-        t = other > t ? other : t;
-      }
-      tile[u] = t;
-      if ((lane & 7) == 0 && g < g_end) {
-        tmax[g >> 3] = t;
-        if (t > W(-INFINITY)) atomicAdd(&hist[abs_bin(t)], 1u);
-      }
-    }
-    // The warp's running maximum, by a reduction over order keys.
-    W run;
-    if constexpr (sizeof(W) == 8) {
-      const uint64_t k = order_key(a.best);
-      const uint32_t hi = __reduce_max_sync(ALL, uint32_t(k >> 32));
-      const uint32_t lo = __reduce_max_sync(ALL, uint32_t(k >> 32) == hi ? uint32_t(k) : 0u);
-      run = key_value((uint64_t(hi) << 32) | lo);
-    } else {
-      run = key_value(__reduce_max_sync(ALL, order_key(a.best)));
-    }
-    const W thr = run - depth;
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int g = g0 + 32 * u + lane;
-      const unsigned leads =
-          __ballot_sync(ALL, (lane & 7) == 0 && g < g_end && tile[u] > W(-INFINITY) && tile[u] >= thr);
-      if (!leads) continue;
-      const int n = __popc(leads);
-      if (count + n > SLOTS) {
-        // Drop the cached tiles that fell below the threshold (order kept);
-        // lane s moves slot s's column of values.
-        __syncwarp();
-        const bool keep = lane < count && c.tmax[lane] >= thr;
-        const unsigned kept = __ballot_sync(ALL, keep);
-        if (kept != (count >= 32 ? ALL : (1u << count) - 1u)) {
-          for (unsigned rest = kept; rest; rest &= rest - 1) {
-            const int src = __ffs(rest) - 1, dst = __popc(kept & ((1u << src) - 1u));
-            if (dst == src) continue;
-            c.val[dst][lane] = c.val[src][lane];
-            if (lane == 0) {
-              c.tmax[dst] = c.tmax[src];
-              c.tile[dst] = c.tile[src];
-            }
-          }
-          __syncwarp();
-        }
-        count = __popc(kept);
-      }
-      const int room = SLOTS - count;
-      const unsigned lead = 1u << (lane & ~7);
-      const int k = __popc(leads & (lead - 1u));
-      if ((leads & lead) && k < room) {
-        const int slot = count + k;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) c.val[slot][4 * (lane & 7) + j] = v[u][j];
-        if ((lane & 7) == 0) {
-          c.tmax[slot] = tile[u];
-          c.tile[slot] = g >> 3;
-        }
-      }
-      count += min(n, room);
-    }
-  }
-  if (lane == 0) *in.cache_count = count;
-  return a;
-}
-
 // One list row's finish by one warp.
 struct ListIn {
   const uint64_t* key;  // m candidates (order keys and token IDs), any order

@@ -306,24 +306,22 @@ template <int DT> struct RowKernel {
     // warps' caches (their count against the rank's own histogram), the
     // gather reads shared memory only.
     bool cached = false;
-    if (r.direct) {
-      auto& tc = r.cache();
-      const int w = warp_id(), lane = lane_id();
-      const int in_cache =
-          __popc(__ballot_sync(0xffffffffu, lane < tc.count[w] && abs_bin(tc.warp[w].tmax[lane]) >= bin));
+    if (!r.resident && r.vec && !r.has_mask) {
+      // Every warp counts alike: this rank's window tiles (its own histogram)
+      // against those in the hot-tile cache.
+      const int lane = lane_id();
+      const int in_cache = __popc(__ballot_sync(0xffffffffu, lane < s.hot_n && abs_bin(s.hot.tmax[lane]) >= bin));
       const int own_top = s.in_stats[r.rank].top_bin;
-      int window_tiles = 0;
+      uint32_t window_tiles = 0;
       for (int k = lane; k <= own_top - bin && k < WIN_BINS; k += 32) window_tiles += s.in_win[r.rank][k];
-      window_tiles = __reduce_add_sync(0xffffffffu, uint32_t(window_tiles));
-      const int have = block_all(lane == 0 ? in_cache : 0, [](int x, int y) { return x + y; }, s.red.ints);
-      cached = have == window_tiles;  // every warp computed window_tiles alike
+      window_tiles = __reduce_add_sync(0xffffffffu, window_tiles);
+      cached = uint32_t(in_cache) == window_tiles;
     }
-    int mine;
+    int mine = 0;
     if (cached) {
-      auto& tc = r.cache();
-      const int w = warp_id();
-      mine = gather_cached_warp<W>(&tc.warp[w].val[0][0], tc.warp[w].tmax, tc.warp[w].tile, tc.count[w], r.lo, bin,
-                                   r.peer(s.u.cand.key, 0), r.peer(s.u.cand.id, 0), r.peer(&s.n_cand, 0), CAP);
+      if (warp_id() == 0)
+        mine = gather_cached_warp<W>(&s.hot.val[0][0], s.hot.tmax, s.hot.tile, s.hot_n, r.lo, bin,
+                                     r.peer(s.u.cand.key, 0), r.peer(s.u.cand.id, 0), r.peer(&s.n_cand, 0), CAP);
     } else {
       const int nt = r.tile_count();
       const int per = (nt + WARPS - 1) / WARPS;
@@ -525,6 +523,8 @@ __global__ void __launch_bounds__(THREADS + (WARM ? 32 : 0), MIN_BLOCKS) rows_ke
   for (int i = threadIdx.x; i < ABS_BINS && int(threadIdx.x) < THREADS; i += THREADS) r.hist_abs[i] = 0;
   if (threadIdx.x == 0) {
     s.n_cand = 0;  // rank 0's candidate counter, before any peer can push (the first cluster exchange)
+    s.hot_n = 0;
+    s.run_key = 0;
     mbar_init(&s.bar, 1);
     for (int i = 0; i < MAX_RING_STAGES; ++i) mbar_init(&s.ring_bar[i], 1);
     mbar_init_fence();
@@ -557,7 +557,7 @@ __global__ void __launch_bounds__(THREADS + (WARM ? 32 : 0), MIN_BLOCKS) rows_ke
   if (stream) {
     if (threadIdx.x == 0) {
       mbar_arrive_expect_tx(&s.bar, 0);
-      if (p.vector_load && !r.direct)  // direct rows read the slice themselves (the ring holds their tile cache)
+      if (p.vector_load)
         for (int c = 0; c < min(p.stream_rows, r.ring_chunks()); ++c) r.ring_issue(c, c);
     }
   } else if (p.vector_load) {
