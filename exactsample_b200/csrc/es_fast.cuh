@@ -216,63 +216,6 @@ __device__ __noinline__ int gather_warp(const SliceRef<T>& src, const W* tmax, i
   return mine;
 }
 
-// gather_warp over tiles held in shared memory: `count` cached tiles, tile s
-// with values val[32 s + lane], maximum cmax[s] and index ctile[s] in the
-// slice (global ID lo + 32 ctile[s] + lane); invalid tokens hold -inf.
-template <class W>
-__device__ __noinline__ int gather_cached_warp(const W* val, const W* cmax, const int32_t* ctile, int count, int lo,
-                                               int bin, uint64_t* keys, int32_t* ids, int* counter, int cap) {
-  constexpr unsigned ALL = 0xffffffffu;
-  constexpr int BATCH = 4;
-  const int lane = lane_id();
-  int mine = 0;
-  int s = 0;
-  while (true) {
-    int slot[BATCH];
-    W v[BATCH];
-    int n = 0;
-    for (; s < count && n < BATCH; ++s) {
-      if (abs_bin(cmax[s]) < bin) continue;
-      slot[n] = s;
-      v[n] = val[32 * s + lane];
-      ++n;
-    }
-    if (n == 0) break;
-    unsigned take[BATCH];
-    int total = 0;
-#pragma unroll
-    for (int b = 0; b < BATCH; ++b) {
-      take[b] = __ballot_sync(ALL, b < n && v[b] > W(-INFINITY) && abs_bin(v[b]) >= bin);
-      total += __popc(take[b]);
-    }
-    if (total == 0) continue;
-    int at0 = 0;
-    if (lane == 0) at0 = atomicAdd(counter, total);
-    at0 = __shfl_sync(ALL, at0, 0);
-#pragma unroll
-    for (int b = 0; b < BATCH; ++b) {
-      if ((take[b] >> lane) & 1u) {
-        const int at_ = at0 + __popc(take[b] & ((1u << lane) - 1u));
-        if (at_ < cap) {
-          keys[at_] = uint64_t(order_key(v[b]));
-          ids[at_] = lo + 32 * ctile[slot[b]] + lane;
-        }
-      }
-      at0 += __popc(take[b]);
-    }
-    mine += total;
-  }
-  return mine;
-}
-
-// A warp's cache of hot tiles (streamed rows): up to SLOTS tiles of 32
-// values (invalid tokens -inf), with each tile's maximum and index.
-template <class W, int SLOTS> struct WarpCache {
-  W val[SLOTS][32];
-  W tmax[SLOTS];
-  int32_t tile[SLOTS];
-};
-
 // One list row's finish by one warp.
 struct ListIn {
   const uint64_t* key;  // m candidates (order keys and token IDs), any order

@@ -302,27 +302,8 @@ template <int DT> struct RowKernel {
                    : SliceRef<T>{r.tbase + int64_t(r.lo) * p.t_s1, p.t_s1,
                                  r.has_mask ? p.mask + int64_t(r.row) * p.m_s0 + int64_t(r.lo >> 5) * p.m_s1 : nullptr,
                                  p.m_s1, r.hi - r.lo, r.lo};
-    // Streamed rows: when every one of this rank's window tiles is in its
-    // warps' caches (their count against the rank's own histogram), the
-    // gather reads shared memory only.
-    bool cached = false;
-    if (!r.resident && r.vec && !r.has_mask) {
-      // Every warp counts alike: this rank's window tiles (its own histogram)
-      // against those in the hot-tile cache.
-      const int lane = lane_id();
-      const int in_cache = __popc(__ballot_sync(0xffffffffu, lane < s.hot_n && abs_bin(s.hot.tmax[lane]) >= bin));
-      const int own_top = s.in_stats[r.rank].top_bin;
-      uint32_t window_tiles = 0;
-      for (int k = lane; k <= own_top - bin && k < WIN_BINS; k += 32) window_tiles += s.in_win[r.rank][k];
-      window_tiles = __reduce_add_sync(0xffffffffu, window_tiles);
-      cached = uint32_t(in_cache) == window_tiles;
-    }
-    int mine = 0;
-    if (cached) {
-      if (warp_id() == 0)
-        mine = gather_cached_warp<W>(&s.hot.val[0][0], s.hot.tmax, s.hot.tile, s.hot_n, r.lo, bin,
-                                     r.peer(s.u.cand.key, 0), r.peer(s.u.cand.id, 0), r.peer(&s.n_cand, 0), CAP);
-    } else {
+    int mine;
+    {
       const int nt = r.tile_count();
       const int per = (nt + WARPS - 1) / WARPS;
       const int t0 = min(nt, warp_id() * per), t1 = min(nt, t0 + per);
@@ -461,7 +442,6 @@ template <int DT> __device__ void warm_up(Smem<typename Types<DT>::W>& s) {
   using W = typename Types<DT>::W;
   struct Dry {
     T row[64];
-    W cval[64];
     W tmax[2];
     uint32_t counts[WIN_BINS];
     uint64_t key[FAST_CAND];
@@ -474,7 +454,6 @@ template <int DT> __device__ void warm_up(Smem<typename Types<DT>::W>& s) {
   // Two tiles of a falling row, 16 down to 8.125 in steps of 1/8.
   for (int h = 0; h < 2; ++h) {
     d.row[lane + 32 * h] = T(16.f - 0.125f * float(lane + 32 * h));
-    d.cval[lane + 32 * h] = W(16.f - 0.125f * float(lane + 32 * h));
   }
   if (lane < 2) d.tmax[lane] = W(16.f - 4.f * float(lane));
   for (int b = lane; b < WIN_BINS; b += 32) d.counts[b] = b < 16 ? 1u : 0u;
@@ -483,12 +462,7 @@ template <int DT> __device__ void warm_up(Smem<typename Types<DT>::W>& s) {
   const int j = window_warp(d.counts, 2);
   const SliceRef<T> src{d.row, 1, nullptr, 0, 64, 0};
   const int bin = abs_bin(W(16)) - max(j, 0) - 8;
-  const int tiles[2] = {0, 1};
-  int m = gather_cached_warp<W>(d.cval, d.tmax, tiles, 2, 0, bin, d.key, d.id, &d.counter, FAST_CAND);
-  __syncwarp();
-  if (lane == 0) d.counter = 0;
-  __syncwarp();
-  m = min(m, gather_warp<T, W>(src, d.tmax, 0, 2, bin, d.key, d.id, &d.counter, FAST_CAND));
+  const int m = gather_warp<T, W>(src, d.tmax, 0, 2, bin, d.key, d.id, &d.counter, FAST_CAND);
   __syncwarp();
   ListIn in{d.key, d.id, min(m, FAST_CAND), 20, 16.0, 0.6, 0.01, 0.95, Address{1u, 2u, 3u, 4u}, 0, -1, nullptr};
   const int sink = finish_warp<W>(in).sample;
@@ -523,8 +497,6 @@ __global__ void __launch_bounds__(THREADS + (WARM ? 32 : 0), MIN_BLOCKS) rows_ke
   for (int i = threadIdx.x; i < ABS_BINS && int(threadIdx.x) < THREADS; i += THREADS) r.hist_abs[i] = 0;
   if (threadIdx.x == 0) {
     s.n_cand = 0;  // rank 0's candidate counter, before any peer can push (the first cluster exchange)
-    s.hot_n = 0;
-    s.run_key = 0;
     mbar_init(&s.bar, 1);
     for (int i = 0; i < MAX_RING_STAGES; ++i) mbar_init(&s.ring_bar[i], 1);
     mbar_init_fence();

@@ -106,9 +106,6 @@ constexpr double MASS_ERR = 1.0e-6;
 // falls back to a full pass.
 constexpr int TILE_CAP = 256;
 
-constexpr int HOT_SLOTS = 32;       // tiles the hot-tile cache holds
-constexpr float HOT_DEPTH = 12.f;   // logits below the running maximum a tile may be and still be cached
-
 template <class W> struct Smem {
   uint64_t bar;
   uint64_t ring_bar[MAX_RING_STAGES];
@@ -152,11 +149,6 @@ template <class W> struct Smem {
   // shared memory.
   Stats<W> in_stats[16];
   uint16_t in_win[16][WIN_BINS];
-  // Streamed rows: the hot-tile cache (Row::post_chunk), its size, and the
-  // order key of the rank's running maximum during the statistics pass.
-  WarpCache<W, HOT_SLOTS> hot;
-  int32_t hot_n;
-  unsigned long long run_key;
   int32_t pushed[16];  // per-rank counts each rank writes into every rank's copy
   int32_t verdict;     // rank 0's decision on a top-p list, written into every rank's copy
   int32_t tiles[TILE_CAP];
@@ -518,20 +510,7 @@ template <int DT> struct Row {
     bulk_columns(reinterpret_cast<uint8_t*>(slice) + stage * RING_CHUNK, lo + int(off / sizeof(T)),
                  int(len / sizeof(T)), bar);
   }
-  // The warp's largest value (every lane), by reductions over order keys.
-  __device__ __forceinline__ static W block_max_warp(W v) {
-    constexpr unsigned ALL = 0xffffffffu;
-    if constexpr (sizeof(W) == 8) {
-      const uint64_t k = order_key(v);
-      const uint32_t hi_ = __reduce_max_sync(ALL, uint32_t(k >> 32));
-      const uint32_t lo_ = __reduce_max_sync(ALL, uint32_t(k >> 32) == hi_ ? uint32_t(k) : 0u);
-      return key_value((uint64_t(hi_) << 32) | lo_);
-    } else {
-      return key_value(__reduce_max_sync(ALL, order_key(v)));
-    }
-  }
-
-  // ---- tile histogram and hot-tile cache ----
+  // ---- tile histogram ----
   // Adds tiles [t0, t1)'s maxima to the absolute histogram: every warp over
   // its share, one atomic per distinct bin per warp step.
   __device__ void hist_tiles(int t0, int t1) {
@@ -543,66 +522,18 @@ template <int DT> struct Row {
       if (b >= 0 && lane_id() == __ffs(same) - 1) atomicAdd(&hist_abs[b], uint32_t(__popc(same)));
     }
   }
-  // Warp 0, after the barrier that ends ring chunk c (its values still in
-  // `stage`, element 0 at local token 32 t0): the histogram of the chunk's
-  // tiles [t0, t1), and a copy of every such tile whose maximum is within
-  // HOT_DEPTH logits of the rank's running maximum into the hot-tile cache
-  // (unmasked rows; when the cache is full, tiles below the threshold are
-  // dropped first, and a tile that still finds no room is not cached). The
-  // list gather reads the window's tiles from the cache when all are there.
-  __device__ void post_chunk(const T* stage, int t0, int t1, int& hot_n) {
-    constexpr unsigned ALL = 0xffffffffu;
-    const int lane = lane_id();
-    const W thr = key_value(Key(s.run_key)) - W(HOT_DEPTH);
-    for (int base = t0; base < t1; base += 32) {
-      const int t = base + lane;
-      const W m = t < t1 ? tmax[t] : W(-INFINITY);
-      const int b = m > W(-INFINITY) ? abs_bin(m) : -1;
-      const unsigned same = __match_any_sync(ALL, b);
-      if (b >= 0 && lane == __ffs(same) - 1) atomicAdd(&hist_abs[b], uint32_t(__popc(same)));
-      if (has_mask) continue;
-      for (unsigned hot = __ballot_sync(ALL, b >= 0 && m >= thr); hot; hot &= hot - 1) {
-        const int tt = base + __ffs(hot) - 1;
-        if (hot_n == HOT_SLOTS) {  // drop the cached tiles that fell below the threshold
-          const unsigned kept = __ballot_sync(ALL, lane < hot_n && s.hot.tmax[lane] >= thr);
-          for (unsigned rest = kept; rest; rest &= rest - 1) {
-            const int src = __ffs(rest) - 1, dst = __popc(kept & ((1u << src) - 1u));
-            if (dst == src) continue;
-            s.hot.val[dst][lane] = s.hot.val[src][lane];
-            if (lane == 0) {
-              s.hot.tmax[dst] = s.hot.tmax[src];
-              s.hot.tile[dst] = s.hot.tile[src];
-            }
-          }
-          hot_n = __popc(kept);
-          __syncwarp();
-          if (hot_n == HOT_SLOTS) break;
-        }
-        s.hot.val[hot_n][lane] = widen(stage[32 * (tt - t0) + lane]);
-        if (lane == 0) {
-          s.hot.tmax[hot_n] = tmax[tt];
-          s.hot.tile[hot_n] = tt;
-        }
-        ++hot_n;
-        __syncwarp();
-      }
-    }
-  }
-
   // The statistics pass over the whole slice: from shared memory (resident),
   // through the TMA ring (streamed, 16-byte aligned rows), or from global
   // memory; then the cluster merge. Returns false if a copy never arrived.
   __device__ bool stats_pass(bool timed_out) {
     Acc a{W(-INFINITY), 0, 0};
     bool lost = timed_out;
-    int hist_from = 0;  // tiles from here on are histogrammed after the pass
     if (resident) {
       stats_groups(0, groups, [&](int g, W v[4]) { load4(slice + 4 * g, v); }, a);
     } else if (vec) {
       constexpr int GPC = int(RING_CHUNK / (4 * sizeof(T)));  // groups per chunk
       const int ring_groups = int(ring_bytes() / (4 * sizeof(T))) & ~7;  // whole tiles
       const int chunks = ring_chunks(), stages = p.stream_rows;
-      int hot_n = 0;  // warp 0: tiles in the hot-tile cache
       for (int c = 0; c < chunks; ++c) {
         uint32_t spins = 0;
         while (!mbar_try_wait(&s.ring_bar[c % stages], uint32_t(c / stages) & 1u))
@@ -611,27 +542,18 @@ template <int DT> struct Row {
             break;
           }
         const T* stage = slice + (c % stages) * (RING_CHUNK / sizeof(T)) - int64_t(c) * GPC * 4;
-        const int g1 = min((c + 1) * GPC, ring_groups);
-        stats_groups(c * GPC, g1, [&](int g, W v[4]) { load4(stage + 4 * g, v); }, a);
-        // The rank's running maximum, for the hot-tile threshold.
-        const W wm = block_max_warp(a.best);
-        if (lane_id() == 0 && wm > W(-INFINITY)) atomicMax(&s.run_key, (unsigned long long)(order_key(wm)));
+        stats_groups(c * GPC, min((c + 1) * GPC, ring_groups),
+                     [&](int g, W v[4]) { load4(stage + 4 * g, v); }, a);
         sync_rows();  // every row thread is done with this stage
-        if (warp_id() == 0) {
-          post_chunk(stage + 4 * c * GPC, c * GPC / 8, g1 / 8, hot_n);
-          __syncwarp();
-          if (lane_id() == 0 && c + stages < chunks) ring_issue(c + stages, c + stages);
-        }
+        if (threadIdx.x == 0 && c + stages < chunks) ring_issue(c + stages, c + stages);
       }
-      if (threadIdx.x == 0) s.hot_n = hot_n;
       ring_seq = chunks;
       stats_groups(ring_groups, groups, [&](int g, W v[4]) { values(g, v); }, a);  // the last partial tile
-      hist_from = ring_groups / 8;
     } else {
       stats_groups(0, groups, [&](int g, W v[4]) { values(g, v); }, a);
     }
     lost = sync_rows_or(lost);
-    hist_tiles(hist_from, tile_count());  // block_stats below syncs before the histogram is read
+    hist_tiles(0, tile_count());  // block_stats below syncs before the histogram is read
     if (lost) a.bad = 1;  // a slice copy never arrived: the row is not trusted
     const int own_top = a.best > W(-INFINITY) ? abs_bin(a.best) : -1;
     const Stats<W> merged = block_stats(Stats<W>{a.best, W(-INFINITY), a.valid, a.bad, 0, 0, own_top});
