@@ -190,7 +190,12 @@ def workload_case(name, requests=None, **kw):
     w = workloads.config(name, **kw)
     if requests is not None:
         w = w.subset(requests)
-    return dict(name=f"{name}" + ("" if requests is None else f"_{len(list(requests))}req"),
+    return case_of(w, f"{name}" + ("" if requests is None else f"_{len(list(requests))}req"))
+
+
+def case_of(w, name):
+    """A workloads.Workload as a case."""
+    return dict(name=name,
                 logits=w.logits, cu_rows=w.cu_rows, draft_ids=w.draft_ids, temperature=w.temperature,
                 top_k=w.top_k, top_p=w.top_p, min_p=w.min_p, draft_kind=w.draft_kind, seed=w.seed,
                 stream_id=w.stream_id, positions=w.positions, mask=w.mask, draft_logits=w.draft_logits,
