@@ -152,66 +152,79 @@ template <class T> struct SliceRef {
 // Appends every valid token of tiles [t0, t1) whose absolute bin is at least
 // `bin` to (keys, ids) from slots reserved on *counter (one atomic per batch
 // of tiles; slots at or past cap are counted but not written). Only tiles
-// whose maximum reaches the bin are read. Returns the number of tokens this
-// warp appended (the same in every lane).
+// whose maximum reaches the bin are read: the warp lists them first (from
+// the tile maxima in shared memory), then loads BATCH of them at a time, all
+// in flight together. Returns the number of tokens this warp appended (the
+// same in every lane).
 template <class T, class W>
 __device__ __noinline__ int gather_warp(const SliceRef<T>& src, const W* tmax, int t0, int t1, int bin,
                                         uint64_t* keys, int32_t* ids, int* counter, int cap) {
   constexpr unsigned ALL = 0xffffffffu;
-  constexpr int BATCH = 4;
+  constexpr int BATCH = 8;
   const int lane = lane_id();
   int mine = 0;
-  for (int base = t0; base < t1; base += 32) {
-    const int t = base + lane;
-    bool hit = false;
-    if (t < t1) {
-      const W m = tmax[t];
-      hit = m > W(-INFINITY) && abs_bin(m) >= bin;
-    }
-    unsigned tiles = __ballot_sync(ALL, hit);
-    while (tiles) {
-      // Up to BATCH listed tiles, all loads in flight before the first use.
-      int tt[BATCH];
-      W v[BATCH];
-#pragma unroll
-      for (int b = 0; b < BATCH; ++b) {
-        tt[b] = -1;
-        v[b] = W(-INFINITY);
-        if (tiles) {
-          tt[b] = base + __ffs(tiles) - 1;
-          tiles &= tiles - 1;
-          const int i = 32 * tt[b] + lane;
-          if (i < src.n) {
-            const bool allowed = src.mask == nullptr ||
-                                 ((uint32_t(src.mask[int64_t(i >> 5) * src.mstride]) >> (i & 31)) & 1u);
-            if (allowed) v[b] = widen(src.values[int64_t(i) * src.vstride]);
-          }
+  int base = t0;
+  unsigned pending = 0;  // hit tiles of the 32 from `base` not yet read
+  while (true) {
+    // The next BATCH listed tiles (warp-uniform).
+    int tt[BATCH];
+    int n = 0;
+    while (n < BATCH) {
+      if (!pending) {
+        if (base >= t1) break;
+        const int t = base + lane;
+        bool hit = false;
+        if (t < t1) {
+          const W m = tmax[t];
+          hit = m > W(-INFINITY) && abs_bin(m) >= bin;
+        }
+        pending = __ballot_sync(ALL, hit);
+        if (!pending) {
+          base += 32;
+          continue;
         }
       }
-      unsigned take[BATCH];
-      int total = 0;
-#pragma unroll
-      for (int b = 0; b < BATCH; ++b) {
-        take[b] = __ballot_sync(ALL, tt[b] >= 0 && v[b] > W(-INFINITY) && abs_bin(v[b]) >= bin);
-        total += __popc(take[b]);
-      }
-      if (total == 0) continue;
-      int slot = 0;
-      if (lane == 0) slot = atomicAdd(counter, total);
-      slot = __shfl_sync(ALL, slot, 0);
-#pragma unroll
-      for (int b = 0; b < BATCH; ++b) {
-        if ((take[b] >> lane) & 1u) {
-          const int at_ = slot + __popc(take[b] & ((1u << lane) - 1u));
-          if (at_ < cap) {
-            keys[at_] = uint64_t(order_key(v[b]));
-            ids[at_] = src.lo + 32 * tt[b] + lane;
-          }
-        }
-        slot += __popc(take[b]);
-      }
-      mine += total;
+      tt[n++] = base + __ffs(pending) - 1;
+      pending &= pending - 1;
+      if (!pending) base += 32;
     }
+    if (n == 0) break;
+    W v[BATCH];
+#pragma unroll
+    for (int b = 0; b < BATCH; ++b) {
+      v[b] = W(-INFINITY);
+      if (b < n) {
+        const int i = 32 * tt[b] + lane;
+        if (i < src.n) {
+          const bool allowed =
+              src.mask == nullptr || ((uint32_t(src.mask[int64_t(i >> 5) * src.mstride]) >> (i & 31)) & 1u);
+          if (allowed) v[b] = widen(src.values[int64_t(i) * src.vstride]);
+        }
+      }
+    }
+    unsigned take[BATCH];
+    int total = 0;
+#pragma unroll
+    for (int b = 0; b < BATCH; ++b) {
+      take[b] = __ballot_sync(ALL, b < n && v[b] > W(-INFINITY) && abs_bin(v[b]) >= bin);
+      total += __popc(take[b]);
+    }
+    if (total == 0) continue;
+    int slot = 0;
+    if (lane == 0) slot = atomicAdd(counter, total);
+    slot = __shfl_sync(ALL, slot, 0);
+#pragma unroll
+    for (int b = 0; b < BATCH; ++b) {
+      if ((take[b] >> lane) & 1u) {
+        const int at_ = slot + __popc(take[b] & ((1u << lane) - 1u));
+        if (at_ < cap) {
+          keys[at_] = uint64_t(order_key(v[b]));
+          ids[at_] = src.lo + 32 * tt[b] + lane;
+        }
+      }
+      slot += __popc(take[b]);
+    }
+    mine += total;
   }
   return mine;
 }
