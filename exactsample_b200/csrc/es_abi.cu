@@ -471,6 +471,9 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
     cluster = choose_cluster(busy, vocab, logits.dtype, full_rows, &p.slice_words, &smem, &p.stream_rows,
                              &p.min_blocks);
     if (cluster < 0) return fail(ES_ERR_UNSUPPORTED, "vocabulary too large for one 16-block cluster's shared memory");
+    // The warm-up warp pays off where rows are split over ranks (one rank
+    // per row leaves the chain after the statistics a smaller share).
+    if (cluster < 2) p.warm = 0;
     const size_t e = element_size(logits.dtype);
     p.vector_load = logits.stride[1] == 1 && reinterpret_cast<uintptr_t>(logits.data) % 16 == 0 &&
                     (uint64_t(logits.stride[0]) * e) % 16 == 0;  // always so for shards (checked above)

@@ -250,36 +250,58 @@ __device__ __forceinline__ bool precedes(uint64_t ka, int32_t ia, uint64_t kb, i
   return ka > kb || (ka == kb && ia < ib);
 }
 
-// Sorts up to 64 (key, id) pairs held two per lane (element e = lane + 32 h)
-// into (key desc, ID asc) order with a bitonic network; empty entries are
-// (0, INT_MAX) and sort last. With `two` false only the first 32 are sorted.
-__device__ __forceinline__ void warp_sort64(uint64_t key[2], int32_t id[2], bool two) {
+// Bitonic sort into (key desc, ID asc) order of N = 32 or 64 entries held
+// N / 32 per lane (entry e = lane + 32 h), fully unrolled. For 32-bit keys
+// the pair is one 64-bit composite, key above (2^32 - 1 - ID), so one
+// comparison orders it; 64-bit keys compare the pair. Empty entries are
+// (0, INT_MAX) and sort last.
+template <int N, bool WIDE> __device__ __forceinline__ void warp_sort(uint64_t key[2], int32_t id[2]) {
   constexpr unsigned ALL = 0xffffffffu;
+  constexpr int H = N / 32;
   const int lane = lane_id();
-  const int top = two ? 64 : 32;
-  for (int k = 2; k <= top; k <<= 1) {
+  uint64_t c[2];
+  if constexpr (!WIDE) {
+#pragma unroll
+    for (int h = 0; h < H; ++h) c[h] = (key[h] << 32) | uint64_t(0xffffffffu - uint32_t(id[h]));
+  }
+#pragma unroll
+  for (int k = 2; k <= N; k <<= 1) {
+#pragma unroll
     for (int j = k >> 1; j > 0; j >>= 1) {
-      if (j == 32) {  // k == 64: elements lane and lane + 32, the whole sequence in order
-        if (precedes(key[1], id[1], key[0], id[0])) {
+      if (j == 32) {  // k == 64: entries lane and lane + 32, the whole sequence descending
+        if constexpr (!WIDE) {
+          if (c[1] > c[0]) {
+            const uint64_t t = c[0]; c[0] = c[1]; c[1] = t;
+          }
+        } else if (precedes(key[1], id[1], key[0], id[0])) {
           const uint64_t tk = key[0]; key[0] = key[1]; key[1] = tk;
           const int32_t ti = id[0]; id[0] = id[1]; id[1] = ti;
         }
         continue;
       }
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        if (h == 1 && !two) break;
+      for (int h = 0; h < H; ++h) {
         const int e = lane + 32 * h;
-        const uint64_t ok = __shfl_xor_sync(ALL, key[h], j);
-        const int32_t oi = __shfl_xor_sync(ALL, id[h], j);
-        const bool lower = (e & j) == 0;
-        const bool desc = (e & k) == 0;
-        const bool mine_first = precedes(key[h], id[h], ok, oi);
-        if (mine_first != (lower == desc)) {
-          key[h] = ok;
-          id[h] = oi;
+        const bool first_here = ((e & j) == 0) == ((e & k) == 0);  // this entry takes the earlier of the pair
+        if constexpr (!WIDE) {
+          const uint64_t o = __shfl_xor_sync(ALL, c[h], j);
+          c[h] = first_here ? (o > c[h] ? o : c[h]) : (o > c[h] ? c[h] : o);
+        } else {
+          const uint64_t ok = __shfl_xor_sync(ALL, key[h], j);
+          const int32_t oi = __shfl_xor_sync(ALL, id[h], j);
+          if (precedes(key[h], id[h], ok, oi) != first_here) {
+            key[h] = ok;
+            id[h] = oi;
+          }
         }
       }
+    }
+  }
+  if constexpr (!WIDE) {
+#pragma unroll
+    for (int h = 0; h < H; ++h) {
+      key[h] = c[h] >> 32;
+      id[h] = int32_t(0xffffffffu - uint32_t(c[h]));
     }
   }
 }
@@ -312,7 +334,9 @@ template <class W> __device__ __noinline__ ListOut finish_warp(const ListIn& in)
     key[h] = e < in.m ? in.key[e] : 0;
     id[h] = e < in.m ? in.id[e] : INT_MAX;
   }
-  warp_sort64(key, id, in.m > 32);
+  constexpr bool WIDE = sizeof(W) == 8;
+  if (in.m > 32) warp_sort<64, WIDE>(key, id);
+  else warp_sort<32, WIDE>(key, id);
   // Lane i holds the i-th token of the order; the first n_keep are kept.
   const bool kept = i < in.n_keep;
   const int tok = kept ? id[0] : INT_MAX;
