@@ -504,6 +504,8 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
 // 512 KiB covers ES_STATIC_MAX_ROWS rows.
 constexpr uint64_t STATIC_SCRATCH_BYTES = 512 * 1024;
 constexpr int MAX_DEVICES = 64;
+static_assert(es::workspace_needed(ES_STATIC_MAX_ROWS) <= STATIC_SCRATCH_BYTES,
+              "the static scratch holds the records of ES_STATIC_MAX_ROWS rows");
 }  // namespace
 
 static __device__ __align__(256) uint8_t es_static_scratch[STATIC_SCRATCH_BYTES];
@@ -553,6 +555,11 @@ int es_verify_timed(const es_args* args, void* stream, void* before, void* after
 int es_verify_static(const es_args* args, void* stream) {
   g_error.clear();
   if (args == nullptr) return fail(ES_ERR_ARGUMENT, "null arguments");
+#ifdef ES_TRACE_PHASES
+  // Phase traces are written past the per-row records, where only a
+  // reference-sized workspace has room.
+  return fail(ES_ERR_UNSUPPORTED, "es_verify_static is not available in a phase-tracing build");
+#endif
   if (args->workspace.ndim != 0 || args->workspace.data != nullptr)
     return fail(ES_ERR_ARGUMENT, "es_verify_static uses its own scratch: leave workspace empty (zeroed)");
   if (args->target_logits.ndim == 2 && args->target_logits.size[0] > ES_STATIC_MAX_ROWS)

@@ -148,7 +148,7 @@ __host__ __device__ inline RowCtx* row_contexts(uint8_t* ws, int64_t rows) {
 
 // Bytes used, whatever the workspace's alignment: at most 8 + 116 * rows + 79,
 // far below the 8 + 12320 * rows provided.
-__host__ __device__ inline uint64_t workspace_needed(int64_t rows) {
+__host__ __device__ constexpr uint64_t workspace_needed(int64_t rows) {
   if (rows == 0) return 8;
   return 8 + uint64_t(rows) * (sizeof(RowResult) + 4) + sizeof(Diagnostics) + 15 + uint64_t(rows) * sizeof(RowCtx);
 }

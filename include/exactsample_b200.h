@@ -127,7 +127,8 @@ int es_verify_timed(const es_args* args, void* stream, void* before, void* after
  * The first call on a device does the set-up: it looks up that device's
  * scratch address (cudaGetSymbolAddress, with the device current), which also
  * loads the library's kernels there. Make that first call before any stream
- * capture.
+ * capture. The address is kept for the life of the process, so resetting the
+ * device (cudaDeviceReset) after that first call is not supported.
  *
  * The scratch needs no clearing between calls: each call's first kernel
  * writes every flag, counter and per-row record that its later kernels read.
