@@ -35,6 +35,10 @@ HEADERS = sorted(CSRC.glob("*.cuh")) + [INCLUDE / "exactsample_b200.h"]
 
 CORE_LIB = PACKAGE / "libexactsample_b200.so"
 TORCH_LIB = PACKAGE / "exactsample_cuda.so"
+# The checked build (-DES_CHECKS: device bounds checks that count failures in
+# the workspace instead of trapping), for the GPU tests' checked run.
+CHECKED_LIB = PACKAGE / "libexactsample_b200_checked.so"
+CHECKED_BUILD = PACKAGE / "_build_checked"
 
 
 def _stale(target: Path, deps) -> bool:
@@ -72,6 +76,26 @@ def build_core(force: bool = False, verbose: bool = False) -> Path:
     return CORE_LIB
 
 
+def build_checked(force: bool = False) -> Path:
+    """libexactsample_b200_checked.so: the C ABI library built with -DES_CHECKS."""
+    CHECKED_BUILD.mkdir(exist_ok=True)
+    objects, jobs = [], []
+    for name in CUDA_SOURCES:
+        src = CSRC / name
+        obj = CHECKED_BUILD / (name + ".o")
+        objects.append(obj)
+        if force or _stale(obj, [src, *HEADERS]):
+            jobs.append([NVCC, *NVCC_FLAGS, "-DES_CHECKS", "-c", str(src), "-o", str(obj)])
+    if jobs:
+        with cf.ThreadPoolExecutor(max_workers=min(len(jobs), os.cpu_count() or 4)) as pool:
+            list(pool.map(_run, jobs))
+    if force or jobs or _stale(CHECKED_LIB, objects):
+        tmp = CHECKED_LIB.with_suffix(".so.tmp")
+        _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objects)])
+        tmp.replace(CHECKED_LIB)
+    return CHECKED_LIB
+
+
 def build_torch_op(force: bool = False) -> Path:
     import torch
     from torch.utils import cpp_extension
@@ -96,7 +120,8 @@ def build_torch_op(force: bool = False) -> Path:
 def build(force: bool = False, verbose: bool = False):
     core = build_core(force, verbose)
     op = build_torch_op(force)
-    return core, op
+    checked = build_checked(force)
+    return core, op, checked
 
 
 def main(argv=None):

@@ -9,7 +9,11 @@ from __future__ import annotations
 import ctypes
 from pathlib import Path
 
-LIBRARY = Path(__file__).with_name("libexactsample_b200.so")
+import os
+
+# $EXACTSAMPLE_ABI_LIBRARY picks another build of the C ABI (the tests' checked
+# run loads libexactsample_b200_checked.so this way).
+LIBRARY = Path(os.environ.get("EXACTSAMPLE_ABI_LIBRARY") or Path(__file__).with_name("libexactsample_b200.so"))
 
 ES_F32, ES_F64, ES_F16, ES_BF16, ES_I32, ES_I64, ES_U8 = range(7)
 ERRORS = {0: "ES_SUCCESS", -1: "ES_ERR_ARGUMENT", -2: "ES_ERR_CAPACITY", -3: "ES_ERR_ALIGNMENT",

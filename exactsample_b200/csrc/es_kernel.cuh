@@ -195,6 +195,7 @@ template <int DT> struct RowKernel {
       return s.ival[3] != 0;
     }
     const int i = threadIdx.x;
+    if (!r.in_bounds(n_keep <= LIST_MAX && m <= CAP, 11)) n_keep = min(n_keep, LIST_MAX);
     const bool in = i < n_keep;
     const int id = in ? s.u.cand.id[i] : INT_MAX;
     double w = 0;
@@ -305,6 +306,7 @@ template <int DT> struct RowKernel {
     int mine;
     {
       const int nt = r.tile_count();
+      if (!r.in_bounds(nt <= (r.p.slice_words * 32 + 31) / 32, 9)) return false;
       const int per = (nt + WARPS - 1) / WARPS;
       const int t0 = min(nt, warp_id() * per), t1 = min(nt, t0 + per);
       mine = gather_warp<T, W>(src, r.tmax, t0, t1, bin, r.peer(s.u.cand.key, 0), r.peer(s.u.cand.id, 0),
@@ -318,6 +320,7 @@ template <int DT> struct RowKernel {
     int m = 0;
     for (int rr = 0; rr < r.ranks; ++rr) m += s.pushed[rr];
     if (m > CAP) return false;  // the block path's radix selection decides
+    if (!r.in_bounds(n_keep <= FAST_KEEP && m >= 0, 10)) return false;
     if (r.rank != 0) return true;
     if (m <= FAST_CAND) {
       if (warp_id() == 0) {

@@ -122,10 +122,13 @@ static_assert(sizeof(RowCtx) == 80, "RowCtx is 80 bytes");
 
 // Counters kept after the per-row arrays (reset by the preparation kernel).
 struct Diagnostics {
-  uint32_t near_ties;      // exact sums whose rounding sat within the fixed-point slack of a tie
-  uint32_t wait_timeouts;  // bounded waits that gave up
-  uint32_t pad[14];
+  uint32_t near_ties;       // exact sums whose rounding sat within the fixed-point slack of a tie
+  uint32_t wait_timeouts;   // bounded waits that gave up
+  uint32_t check_failures;  // checked builds (-DES_CHECKS): bounds checks that failed (their access skipped)
+  uint32_t first_site;      // checked builds: the site number of the first failed check
+  uint32_t pad[12];
 };
+static_assert(sizeof(Diagnostics) == 64, "Diagnostics is 64 bytes");
 
 // Workspace (bytes): [0] malformed-offsets flag, [4] FP64 recomputation count,
 // [8] RowResult[rows], then one arrival counter per row (used at each
@@ -154,6 +157,18 @@ __host__ __device__ constexpr uint64_t workspace_needed(int64_t rows) {
 }
 
 template <class T> __device__ __forceinline__ T at(const T* p, int64_t stride, int64_t i) { return p[i * stride]; }
+
+// Bounds checks of checked builds (-DES_CHECKS), the stand-in for a memory
+// checker where none may run: ES_IN_BOUNDS(ws, rows, cond, site) is cond;
+// a false cond adds one to the workspace's check_failures, records the first
+// failing site, and the caller skips the access. Nothing traps. In other
+// builds the macro is `true` and costs nothing.
+#ifdef ES_CHECKS
+static __device__ __noinline__ void check_failed(uint8_t* ws, int64_t rows, uint32_t site);
+#define ES_IN_BOUNDS(ws, rows, cond, site) ((cond) ? true : (es::check_failed((ws), (rows), (site)), false))
+#else
+#define ES_IN_BOUNDS(ws, rows, cond, site) true
+#endif
 
 // Phase timestamps for development builds (-DES_TRACE_PHASES): rank r of row
 // `row` stores %globaltimer at phase k in the workspace past every record

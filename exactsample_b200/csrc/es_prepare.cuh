@@ -8,6 +8,14 @@
 
 namespace es {
 
+#ifdef ES_CHECKS
+static __device__ __noinline__ void check_failed(uint8_t* ws, int64_t rows, uint32_t site) {
+  Diagnostics* d = diagnostics(ws, rows);
+  atomicAdd(&d->check_failures, 1u);
+  atomicCAS(&d->first_site, 0u, site);
+}
+#endif
+
 // Whether cu_rows is malformed: cu[0] != 0, cu[R] != rows, or a pair out of
 // order or out of range. The whole block computes it.
 __device__ inline bool offsets_malformed(const Params& p) {

@@ -368,6 +368,10 @@ template <int DT> struct Row {
     return weight_kept_fp64(double(v), double(maxv), temperature, min_p);
   }
 
+  __device__ __forceinline__ bool in_bounds(bool cond, int site) const {
+    return ES_IN_BOUNDS(p.workspace, p.rows, cond, uint32_t(site));
+  }
+
   __device__ void count_fallback() {
     if (rank == 0 && threadIdx.x == 0) atomicAdd(fallback_count(p.workspace), 1u);
   }
@@ -453,7 +457,8 @@ template <int DT> struct Row {
         const W other = shfl_xor(tile, o);
         tile = other > tile ? other : tile;
       }
-      if ((lane_id() & 7) == 0 && g < g_end) tmax[g >> 3] = tile;
+      if ((lane_id() & 7) == 0 && g < g_end && in_bounds(unsigned(g >> 3) < unsigned(tile_count()), 1))
+        tmax[g >> 3] = tile;
     }
   }
   // Tiles (32 tokens) of this rank's slice; the last may be partial.
@@ -461,6 +466,7 @@ template <int DT> struct Row {
   // Local token i of the slice (0 <= i < hi - lo): its value and whether the
   // mask allows it.
   __device__ __forceinline__ W value_local(int i) const {
+    if (resident && !in_bounds(unsigned(i) < unsigned(p.slice_words * 32), 7)) return W(-INFINITY);
     return resident ? widen(slice[i]) : widen(*target_at(lo + i));
   }
   __device__ __forceinline__ bool allowed_local(int i) const {
@@ -519,7 +525,8 @@ template <int DT> struct Row {
       const W m = t < t1 ? tmax[t] : W(-INFINITY);
       const int b = m > W(-INFINITY) ? abs_bin(m) : -1;
       const unsigned same = __match_any_sync(0xffffffffu, b);
-      if (b >= 0 && lane_id() == __ffs(same) - 1) atomicAdd(&hist_abs[b], uint32_t(__popc(same)));
+      if (b >= 0 && lane_id() == __ffs(same) - 1 && in_bounds(b < ABS_BINS, 4))
+        atomicAdd(&hist_abs[b], uint32_t(__popc(same)));
     }
   }
   // The statistics pass over the whole slice: from shared memory (resident),
@@ -529,7 +536,9 @@ template <int DT> struct Row {
     Acc a{W(-INFINITY), 0, 0};
     bool lost = timed_out;
     if (resident) {
-      stats_groups(0, groups, [&](int g, W v[4]) { load4(slice + 4 * g, v); }, a);
+      stats_groups(0, groups, [&](int g, W v[4]) {
+        if (in_bounds(4 * g + 4 <= p.slice_words * 32, 2)) load4(slice + 4 * g, v);
+      }, a);
     } else if (vec) {
       constexpr int GPC = int(RING_CHUNK / (4 * sizeof(T)));  // groups per chunk
       const int ring_groups = int(ring_bytes() / (4 * sizeof(T))) & ~7;  // whole tiles
@@ -542,8 +551,9 @@ template <int DT> struct Row {
             break;
           }
         const T* stage = slice + (c % stages) * (RING_CHUNK / sizeof(T)) - int64_t(c) * GPC * 4;
-        stats_groups(c * GPC, min((c + 1) * GPC, ring_groups),
-                     [&](int g, W v[4]) { load4(stage + 4 * g, v); }, a);
+        stats_groups(c * GPC, min((c + 1) * GPC, ring_groups), [&](int g, W v[4]) {
+          if (in_bounds(g >= c * GPC && g < (c + 1) * GPC && c % stages < MAX_RING_STAGES, 3)) load4(stage + 4 * g, v);
+        }, a);
         sync_rows();  // every row thread is done with this stage
         if (threadIdx.x == 0 && c + stages < chunks) ring_issue(c + stages, c + stages);
       }
@@ -560,7 +570,8 @@ template <int DT> struct Row {
     // Store the statistics and the WIN_BINS tile-maximum bins from this
     // rank's top bin down into every rank's inbox (the histogram is
     // complete: block_stats synced); the exchange orders the stores.
-    if (int(threadIdx.x) < ranks) *peer(&s.in_stats[rank], threadIdx.x) = merged;
+    if (int(threadIdx.x) < ranks && in_bounds(ranks <= 16 && rank < ranks, 5))
+      *peer(&s.in_stats[rank], threadIdx.x) = merged;
     if (int(threadIdx.x) < WIN_BINS) {
       const int b = merged.top_bin - int(threadIdx.x);
       const uint16_t n = uint16_t(merged.top_bin >= 0 && b >= 0 ? min(hist_abs[b], 65535u) : 0u);
@@ -587,7 +598,9 @@ template <int DT> struct Row {
       uint32_t n = 0;
       for (int r = 0; r < ranks; ++r) {
         const int shift = top_bin - s.in_stats[r].top_bin;  // >= 0
-        if (s.in_stats[r].top_bin >= 0 && int(threadIdx.x) >= shift) n += s.in_win[r][threadIdx.x - shift];
+        if (s.in_stats[r].top_bin >= 0 && int(threadIdx.x) >= shift &&
+            in_bounds(int(threadIdx.x) - shift < WIN_BINS, 6))
+          n += s.in_win[r][threadIdx.x - shift];
       }
       s.win[threadIdx.x] = n;
     }
@@ -987,6 +1000,7 @@ template <int DT> struct Row {
   // Sorts rank 0's m candidates into (key desc, ID asc) order (bitonic):
   // up to 32 within warp 0's registers, more in shared memory.
   __device__ void sort_candidates(int m) {
+    if (!in_bounds(m <= CAP, 8)) m = CAP;
     if (m <= 32) {
       if (warp_id() == 0) {
         const int i = lane_id();

@@ -61,15 +61,47 @@ def device_inputs(case, *, dtype=None, strided=False, max_draft=None, reference=
     return t
 
 
+# Workspace poison: every call through run_abi starts from a workspace filled
+# with this byte (the kernels must initialise whatever they read), and after
+# the call the bytes past the records the call may use must still hold it.
+POISON = 0xA5
+
+
+def workspace_records(rows: int) -> int:
+    """An upper bound on the workspace bytes a call over `rows` target rows
+    uses: the 8-byte header, a 32-byte result and a 4-byte arrival counter
+    per row, 64 bytes of diagnostics, up to 15 bytes of alignment and an
+    80-byte context record per row (exactsample_b200/csrc/es_layout.cuh)."""
+    return 8 if rows == 0 else 8 + rows * 36 + 64 + 15 + rows * 80
+
+
+def diagnostics(t):
+    """The workspace's diagnostic counters: near_ties, wait_timeouts,
+    check_failures and first_site (checked builds count failed bounds checks)."""
+    rows = t["target_logits"].shape[0]
+    at = 8 + rows * 36
+    d = t["workspace"][at:at + 16].cpu().numpy().view(np.uint32)
+    return dict(near_ties=int(d[0]), wait_timeouts=int(d[1]), check_failures=int(d[2]), first_site=int(d[3]))
+
+
 def run_abi(t, *, mode="ratio", dispatch="fused", list_max=256):
-    """One call through the C ABI; returns numpy (tokens, accepted, status, path)."""
+    """One call through the C ABI on a poisoned workspace; checks that nothing
+    was written past the call's records and that no bounds check failed
+    (in a checked build); returns numpy (tokens, accepted, status, path)."""
     import torch
     from exactsample_b200 import capi
 
+    ws = t["workspace"]
+    ws.fill_(POISON)
     capi.call({k: v for k, v in t.items() if not k.startswith("_")}, mode={"ratio": 0, "coupled": 1}[mode],
               dispatch={"auto": 0, "reference": 1, "fused": 2}[dispatch], max_draft=t["_max_draft"],
               list_max=list_max)
     torch.cuda.synchronize()
+    tail = ws[workspace_records(t["target_logits"].shape[0]):]
+    assert bool((tail == POISON).all()), "a call wrote past its workspace records"
+    if t["cu_rows"].numel() > 1 and t["target_logits"].shape[0] > 0:
+        d = diagnostics(t)
+        assert d["check_failures"] == 0 and d["wait_timeouts"] == 0, d
     return outputs(t)
 
 
