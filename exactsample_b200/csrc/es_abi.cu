@@ -119,6 +119,11 @@ __global__ void finish_flags(uint64_t* mine, const __grid_constant__ FlagSet f) 
 }
 
 template <int DT> cudaError_t launch_rows(const Params& p, int cluster, cudaStream_t stream);
+template <int DT> cudaError_t launch_reference(const Params& p, cudaStream_t stream);
+extern template cudaError_t launch_reference<ES_F32>(const Params&, cudaStream_t);
+extern template cudaError_t launch_reference<ES_F64>(const Params&, cudaStream_t);
+extern template cudaError_t launch_reference<ES_F16>(const Params&, cudaStream_t);
+extern template cudaError_t launch_reference<ES_BF16>(const Params&, cudaStream_t);
 extern template cudaError_t launch_rows<ES_F32>(const Params&, int, cudaStream_t);
 extern template cudaError_t launch_rows<ES_F64>(const Params&, int, cudaStream_t);
 extern template cudaError_t launch_rows<ES_F16>(const Params&, int, cudaStream_t);
@@ -482,7 +487,22 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
   if (!p.offsets_inline) es::check_offsets<<<1, 1024, 0, stream>>>(p);
   es::prepare<<<unsigned((requests + 127) / 128), 128, 0, stream>>>(p);
   cudaError_t e = cudaGetLastError();
-  if (e == cudaSuccess && rows > 0) {
+  // dispatch="reference": the independent FP64 kernel (es_reference.cuh),
+  // whose per-row scratch a reference-sized workspace always holds; a
+  // smaller scratch (es_verify_static) takes the fused kernel's FP64-only draws.
+  const uint64_t ws_bytes = own_scratch ? own_scratch : uint64_t(ws.size[0]);
+  const bool reference_kernel = p.exact_draws && sh == nullptr &&
+                                ws_bytes >= es::reference_scratch_offset(rows) + es::reference_scratch_bytes(rows, vocab);
+  if (e == cudaSuccess && rows > 0 && reference_kernel) {
+    if (before != nullptr) cudaEventRecord(before, stream);
+    switch (logits.dtype) {
+      case ES_F32: e = es::launch_reference<ES_F32>(p, stream); break;
+      case ES_F64: e = es::launch_reference<ES_F64>(p, stream); break;
+      case ES_F16: e = es::launch_reference<ES_F16>(p, stream); break;
+      default: e = es::launch_reference<ES_BF16>(p, stream); break;
+    }
+    if (after != nullptr) cudaEventRecord(after, stream);
+  } else if (e == cudaSuccess && rows > 0) {
     if (before != nullptr) cudaEventRecord(before, stream);
     switch (logits.dtype) {
       case ES_F32: e = es::launch_rows<ES_F32>(p, cluster, stream); break;

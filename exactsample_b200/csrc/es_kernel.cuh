@@ -1,5 +1,6 @@
 // The row kernel's body (one cluster per row) and its launcher.
 #pragma once
+#include "es_reference.cuh"
 #include "es_rows.cuh"
 
 namespace es {
@@ -657,6 +658,12 @@ template <int DT> cudaError_t launch_rows(const Params& p, int cluster, cudaStre
   config.attrs = attrs;
   config.numAttrs = 2;
   return cudaLaunchKernelEx(&config, kernel, p);
+}
+
+// Launch of the independent FP64 kernel (dispatch="reference"): one block per row.
+template <int DT> cudaError_t launch_reference(const Params& p, cudaStream_t stream) {
+  reference_rows<DT><<<unsigned(p.rows), REF_THREADS, 0, stream>>>(p);
+  return cudaGetLastError();
 }
 
 }  // namespace es

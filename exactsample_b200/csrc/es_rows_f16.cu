@@ -4,4 +4,5 @@
 
 namespace es {
 template cudaError_t launch_rows<ES_F16>(const Params&, int, cudaStream_t);
+template cudaError_t launch_reference<ES_F16>(const Params&, cudaStream_t);
 }  // namespace es
