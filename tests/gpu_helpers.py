@@ -97,7 +97,11 @@ def run_abi(t, *, mode="ratio", dispatch="fused", list_max=256):
               dispatch={"auto": 0, "reference": 1, "fused": 2}[dispatch], max_draft=t["_max_draft"],
               list_max=list_max)
     torch.cuda.synchronize()
-    tail = ws[workspace_records(t["target_logits"].shape[0]):]
+    rows, vocab = t["target_logits"].shape
+    used = workspace_records(rows)
+    if dispatch == "reference":  # the FP64 kernel's scratch: 16 bytes per token per row, 16-byte aligned
+        used = (used + 15) // 16 * 16 + rows * vocab * 16
+    tail = ws[used:]
     assert bool((tail == POISON).all()), "a call wrote past its workspace records"
     if t["cu_rows"].numel() > 1 and t["target_logits"].shape[0] > 0:
         d = diagnostics(t)

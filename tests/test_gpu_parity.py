@@ -89,6 +89,18 @@ def test_benchmark_configuration_full_size(name):
         assert (expected[2] == 2).all()  # coupled mode with full proposals is invalid by contract
 
 
+@pytest.mark.parametrize("name", ["C1", "C2a", "C2b", "C3a", "C3b_ratio_full", "C3b_coupled_onehot", "C4"])
+def test_reference_dispatch_full_size(name):
+    """dispatch="reference" runs the independent FP64 kernel (one block per
+    row); it must agree with the oracle at full vocabulary, and so with the
+    fused kernel."""
+    case = C.workload_case(name)
+    expected = oracle_outputs(case)
+    got = run_abi(device_inputs(case, reference=True), mode=case["mode"], dispatch="reference")
+    assert_same(got, expected, context=f"{name} reference dispatch")
+    assert (got[3][:len(expected[2])] == 0).all()  # path_used: reference
+
+
 @pytest.mark.parametrize("setting", ["qwen", "temperature", "top_p"])
 def test_sampler_grid_settings(setting):
     """The three settings of the reference's sampler benchmark grid
