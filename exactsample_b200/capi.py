@@ -20,7 +20,7 @@ ERRORS = {0: "ES_SUCCESS", -1: "ES_ERR_ARGUMENT", -2: "ES_ERR_CAPACITY", -3: "ES
           -4: "ES_ERR_ALIAS", -5: "ES_ERR_UNSUPPORTED", -6: "ES_ERR_LAUNCH", -7: "ES_ERR_DEVICE"}
 # Every function the header declares.
 EXPORTS = ["es_workspace_bytes", "es_verify", "es_verify_timed", "es_verify_static", "es_verify_sharded",
-           "es_shard_signal", "es_shard_wait", "es_shard_finish", "es_ipc_alloc", "es_ipc_open", "es_ipc_close", "es_ipc_free",
+           "es_shard_exchange_bytes", "es_shard_signal", "es_shard_wait", "es_shard_finish", "es_ipc_alloc", "es_ipc_open", "es_ipc_close", "es_ipc_free",
            "es_last_error", "es_abi_version"]
 MAX_SHARDS = 8  # ES_MAX_SHARDS
 STATIC_MAX_ROWS = 4096  # ES_STATIC_MAX_ROWS
@@ -48,7 +48,9 @@ class Shards(ctypes.Structure):
                 ("vocab", ctypes.c_int64), ("req_begin", ctypes.c_int64), ("req_end", ctypes.c_int64),
                 ("epoch", ctypes.c_uint64)] + [
         (name, ctypes.c_void_p * MAX_SHARDS)
-        for name in ["target", "draft", "tokens", "accepted", "status", "path", "ready"]]
+        for name in ["target", "draft", "tokens", "accepted", "status", "path", "ready"]] + [
+        ("phases", ctypes.c_int32), ("pad", ctypes.c_int32), ("exchange", ctypes.c_void_p * MAX_SHARDS),
+        ("scratch", ctypes.c_void_p)]
 
 
 _lib = None
@@ -73,6 +75,8 @@ def load(path: str | Path | None = None) -> ctypes.CDLL:
         lib.es_verify_static.restype = ctypes.c_int
         lib.es_verify_sharded.argtypes = [ctypes.POINTER(Args), ctypes.POINTER(Shards), ctypes.c_void_p]
         lib.es_verify_sharded.restype = ctypes.c_int
+        lib.es_shard_exchange_bytes.argtypes = [ctypes.c_int64, ctypes.POINTER(ctypes.c_uint64)]
+        lib.es_shard_exchange_bytes.restype = ctypes.c_int
         lib.es_shard_signal.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]
         lib.es_shard_signal.restype = ctypes.c_int
         lib.es_shard_wait.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, ctypes.c_uint64,

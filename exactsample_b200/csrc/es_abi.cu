@@ -319,6 +319,8 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
     if (logits.size[1] != width) return fail(ES_ERR_ARGUMENT, "shards: target_logits must be this GPU's shard [rows, its columns]");
     if (!(sh->req_begin >= 0 && sh->req_begin <= sh->req_end && sh->req_end <= requests))
       return fail(ES_ERR_ARGUMENT, "shards: the request range must lie in [0, requests]");
+    if (sh->phases && !(sh->req_begin == 0 && sh->req_end == requests))
+      return fail(ES_ERR_ARGUMENT, "shards: a per-phase call finishes every request on every GPU");
     vocab = sh->vocab;
   }
   if (requests == 0 && rows != 0) return fail(ES_ERR_ARGUMENT, "an empty request batch cannot contain target rows");
@@ -412,6 +414,13 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
     }
     if (has_draft) aligned &= a->draft_logits.stride[1] == 1 && a->draft_logits.stride[0] == logits.stride[0];
     if (!aligned) return fail(ES_ERR_ALIGNMENT, "shards: shard buffers must be contiguous rows on 16-byte boundaries");
+    if (sh->phases) {
+      for (int g = 0; g < sh->count; ++g)
+        if (sh->exchange[g] == nullptr || reinterpret_cast<uintptr_t>(sh->exchange[g]) % 16 != 0)
+          return fail(ES_ERR_ARGUMENT, "shards: a per-phase call needs every GPU's exchange buffer (16-byte aligned)");
+      if (sh->scratch == nullptr || reinterpret_cast<uintptr_t>(sh->scratch) % 16 != 0)
+        return fail(ES_ERR_ARGUMENT, "shards: a per-phase call needs this GPU's scratch (16-byte aligned)");
+    }
   }
   if (requests == 0) return ES_SUCCESS;
   const int dev = device_check();
@@ -442,7 +451,13 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
   p.exact_draws = a->dispatch == ES_REFERENCE;
   p.list_max = p.exact_draws ? 0 : int32_t(a->list_max);
   p.offsets_inline = requests <= 8192;
-  p.fast = !p.exact_draws && p.list_max > 0 && sh == nullptr;
+  p.fast = !p.exact_draws && p.list_max > 0 && (sh == nullptr || sh->phases);
+  p.col0 = 0;
+  p.width = int32_t(vocab);
+  if (sh != nullptr && sh->phases) {
+    p.col0 = int32_t(int64_t(sh->rank) * sh->cols);
+    p.width = int32_t(logits.size[1]);
+  }
   p.warm = p.fast;
   if (const char* forced = std::getenv("EXACTSAMPLE_FAST")) {  // 0: the block-level list path only; 1: no warm-up warp
     if (forced[0] == '0') p.fast = p.warm = 0;
@@ -456,6 +471,8 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
     t.req_begin = int32_t(sh->req_begin);
     t.req_end = int32_t(sh->req_end);
     t.epoch = sh->epoch;
+    t.phases = sh->phases != 0;
+    t.scratch = static_cast<uint8_t*>(sh->scratch);
     for (int g = 0; g < sh->count; ++g) {
       t.target[g] = sh->target[g];
       t.draft[g] = has_draft ? sh->draft[g] : nullptr;
@@ -464,16 +481,19 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
       t.status[g] = static_cast<int32_t*>(sh->status[g]);
       t.path[g] = static_cast<int32_t*>(sh->path[g]);
       t.ready[g] = sh->ready[g];
+      t.exchange[g] = static_cast<uint8_t*>(sh->exchange[g]);
     }
   }
 
   int cluster = 1;
   size_t smem = 0;
   if (rows > 0) {
-    // A sharded call finishes about rows / count of the rows on this GPU.
-    const int64_t busy = sh != nullptr ? (rows + sh->count - 1) / sh->count : rows;
+    // A column-pulling sharded call finishes about rows / count of the rows
+    // on this GPU; a per-phase one every row over this GPU's columns.
+    const bool pulls = sh != nullptr && !sh->phases;
+    const int64_t busy = pulls ? (rows + sh->count - 1) / sh->count : rows;
     const bool full_rows = p.exact_draws || a->list_max == 0;
-    cluster = choose_cluster(busy, vocab, logits.dtype, full_rows, &p.slice_words, &smem, &p.stream_rows,
+    cluster = choose_cluster(busy, p.width, logits.dtype, full_rows, &p.slice_words, &smem, &p.stream_rows,
                              &p.min_blocks);
     if (cluster < 0) return fail(ES_ERR_UNSUPPORTED, "vocabulary too large for one 16-block cluster's shared memory");
     // The warm-up warp pays off where rows are split over ranks (one rank
@@ -603,6 +623,13 @@ int es_verify_sharded(const es_args* args, const es_shards* shards, void* stream
     return ES_ERR_ARGUMENT;
   }
   return verify_impl(args, static_cast<cudaStream_t>(stream), nullptr, nullptr, 0, shards);
+}
+
+int es_shard_exchange_bytes(int64_t rows, uint64_t* bytes) {
+  g_error.clear();
+  if (rows < 0 || bytes == nullptr) return fail(ES_ERR_ARGUMENT, "invalid exchange shape");
+  *bytes = uint64_t(rows) * sizeof(es::PhaseRow);
+  return ES_SUCCESS;
 }
 
 int es_shard_signal(uint64_t* flag, uint64_t epoch, void* stream) {

@@ -321,6 +321,24 @@ __device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
 __device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+// System-scope loads of words a peer GPU publishes (after the acquire of
+// its flag and fence_acq_rel_sys), never served from a stale L1 line.
+__device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint16_t ld_relaxed_sys(const uint16_t* p) {
+  uint16_t v;
+  asm volatile("ld.relaxed.sys.global.u16 %0, [%1];" : "=h"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 // Programmatic dependent launch: the row kernel starts its loads while the
 // preparation kernel runs, and waits for it before reading what it wrote.
 __device__ __forceinline__ void wait_for_prerequisite_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

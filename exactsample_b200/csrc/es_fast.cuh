@@ -79,6 +79,7 @@ constexpr int ABS_ZERO = 512;
 constexpr int WIN_BINS = 128;  // bins a rank publishes, from its own top bin down
 constexpr int FAST_CAND = 64;  // candidates the warp sort takes (two per lane)
 constexpr int FAST_KEEP = 32;  // kept tokens the warp finish takes (one per lane)
+static_assert(WIN_BINS == PHASE_BINS, "a per-phase record carries one cluster window");
 
 __device__ __forceinline__ int abs_bin(float v) {
   const float b = fminf(fmaxf(floorf(__fmul_rn(v, 2.f)), -float(ABS_ZERO)), float(ABS_BINS - ABS_ZERO - 1));

@@ -298,12 +298,14 @@ template <int DT> struct RowKernel {
     ES_TRACE(p.workspace, p.rows, r.row, r.rank, 4);
     if (j < 0) return false;
     const int bin = r.top_bin - j;
+    // Token IDs are global: a per-phase shard's columns start at p.col0
+    // (such calls take this path only without a mask).
     const SliceRef<T> src =
         r.resident ? SliceRef<T>{r.slice, 1, r.has_mask ? reinterpret_cast<const int32_t*>(r.mask_s) : nullptr, 1,
-                                 r.hi - r.lo, r.lo}
+                                 r.hi - r.lo, p.col0 + r.lo}
                    : SliceRef<T>{r.tbase + int64_t(r.lo) * p.t_s1, p.t_s1,
                                  r.has_mask ? p.mask + int64_t(r.row) * p.m_s0 + int64_t(r.lo >> 5) * p.m_s1 : nullptr,
-                                 p.m_s1, r.hi - r.lo, r.lo};
+                                 p.m_s1, r.hi - r.lo, p.col0 + r.lo};
     int mine;
     {
       const int nt = r.tile_count();
@@ -320,10 +322,17 @@ template <int DT> struct RowKernel {
     ES_TRACE(p.workspace, p.rows, r.row, r.rank, 5);
     int m = 0;
     for (int rr = 0; rr < r.ranks; ++rr) m += s.pushed[rr];
-    if (m > CAP) return false;  // the block path's radix selection decides
-    if (!r.in_bounds(n_keep <= FAST_KEEP && m >= 0, 10)) return false;
-    if (r.rank != 0) return true;
-    if (m <= FAST_CAND) {
+    if (r.phases) {
+      if (r.rank != 0) return true;  // rank 0 finishes the row
+      m = phase_candidates(r, m);
+      if (m == -2) return true;  // a peer never published: the row is marked invalid
+      if (m < 0) return false;   // too many candidates: rank 0 finishes the row in FP64
+    } else {
+      if (m > CAP) return false;  // the block path's radix selection decides
+      if (r.rank != 0) return true;
+    }
+    if (!r.in_bounds(n_keep <= LIST_MAX && m >= 0 && m <= CAP, 10)) return false;
+    if (m <= FAST_CAND && n_keep <= FAST_KEEP) {
       if (warp_id() == 0) {
         const ListIn in{s.u.cand.key, s.u.cand.id, m, n_keep, double(r.maxv), r.temperature, r.min_p, r.top_p,
                         r.addr, verify ? 1 : 0, c.draft_id, &diagnostics(p.workspace, p.rows)->near_ties};
@@ -337,6 +346,81 @@ template <int DT> struct RowKernel {
       list_finish(r, c, m, n_keep, verify, false, 0.0, res, Interval{0, 0});
     }
     return true;
+  }
+
+  // Per-phase sharded calls, rank 0 after its cluster's gather: publishes
+  // this GPU's m window candidates (global token IDs) in its exchange
+  // record, waits for every GPU's, and assembles them all in GPU order in
+  // the candidate buffer. Returns their number; -1 when they do not fit
+  // (the row is then finished in FP64, the same decision on every GPU);
+  // -2 when a peer never published.
+  __device__ static int phase_candidates(R& r, int m) {
+    auto& s = r.s;
+    const Params& p = r.p;
+    PhaseRow* mine = r.phase_row(p.sh.rank);
+    const int n = m <= CAP ? m : CAP + 1;
+    for (int i = threadIdx.x; i < min(n, CAP); i += THREADS) {
+      mine->key[i] = s.u.cand.key[i];
+      mine->id[i] = s.u.cand.id[i];
+    }
+    if (threadIdx.x == 0) mine->n_cand = n;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      st_release_sys(&mine->flag_cands, p.sh.epoch);
+    }
+    if (!r.phase_wait(true)) return -2;
+    if (threadIdx.x == 0) {
+      int total = 0, ok = 1;
+      for (int g = 0; g < p.sh.count; ++g) {
+        const int ng = int(ld_relaxed_sys(reinterpret_cast<const uint32_t*>(&r.phase_row(g)->n_cand)));
+        s.pushed[g] = total;
+        s.peer_n[g] = uint32_t(ng);
+        if (ng > CAP) ok = 0;
+        else total += ng;
+      }
+      s.ival[3] = ok && total <= CAP ? total : -1;
+    }
+    __syncthreads();
+    const int total = s.ival[3];
+    if (total < 0) return -1;
+    for (int g = 0; g < p.sh.count; ++g) {
+      const PhaseRow* q = r.phase_row(g);
+      const int ng = int(s.peer_n[g]), off = s.pushed[g];
+      for (int i = threadIdx.x; i < ng; i += THREADS) {
+        s.u.cand.key[off + i] = ld_relaxed_sys(&q->key[i]);
+        s.u.cand.id[off + i] = int32_t(ld_relaxed_sys(reinterpret_cast<const uint32_t*>(&q->id[i])));
+      }
+    }
+    __syncthreads();
+    return total;
+  }
+
+  // Per-phase sharded calls: the whole row in FP64 (es_reference.cuh) by
+  // rank 0 alone, reading every GPU's shard, for rows the exchange cannot
+  // finish. The same on every GPU.
+  __device__ static RowResult phase_fp64(R& r, const RowCtx& c) {
+    const Params& p = r.p;
+    static_assert(sizeof(RefShared) <= sizeof(decltype(r.s.u)), "the FP64 path's shared state fits the candidate buffer");
+    RefShared& rs = *reinterpret_cast<RefShared*>(&r.s.u);
+    double* w = reinterpret_cast<double*>(p.sh.scratch) + int64_t(r.row) * p.vocab * 2;
+    uint64_t* keys = reinterpret_cast<uint64_t*>(w + p.vocab);
+    const int row = r.row;
+    return reference_row<THREADS>(
+        p, row, c,
+        [&](int t) {
+          const int g = t / p.sh.cols;
+          return double(widen(static_cast<const T*>(p.sh.target[g])[int64_t(row) * p.t_s0 + int64_t(t - g * p.sh.cols) * p.t_s1]));
+        },
+        [&](int t) {
+          return p.mask == nullptr ||
+                 ((uint32_t(p.mask[int64_t(row) * p.m_s0 + int64_t(t >> 5) * p.m_s1]) >> (t & 31)) & 1u);
+        },
+        [&](int t) {
+          const int g = t / p.sh.cols;
+          return double(widen(static_cast<const T*>(p.sh.draft[g])[int64_t(row) * p.q_s0 + int64_t(t - g * p.sh.cols) * p.q_s1]));
+        },
+        w, keys, rs);
   }
 
   // Returns true when rank 0 finishes the row alone (a list row): the other
@@ -581,6 +665,43 @@ __global__ void __launch_bounds__(THREADS + (WARM ? 32 : 0), MIN_BLOCKS) rows_ke
   r.top_p = c.top_p;
   r.min_p = c.min_p;
   r.addr = Address{c.stream, c.position, uint32_t(c.seed), uint32_t(c.seed >> 32)};
+  if (r.phases) {
+    // A per-phase sharded call: the row's statistics over every GPU, then
+    // the list path with the candidates exchanged, or FP64 over the whole row.
+    RowResult res{ES_OK, ES_OK, 0, -1, -1, {0, 0, 0}};
+    bool done = !r.phase_stats();  // a peer that never published leaves the row invalid
+    if (!done) {
+      const int valid = r.all.valid;
+      const int n_keep = (c.top_k > 0 && c.top_k < valid) ? int(c.top_k) : valid;
+      const bool listed = !r.all.bad && valid > 0 && c.temperature > 0 && !full_q && !p.exact_draws &&
+                          !r.has_mask && p.fast && n_keep < valid && n_keep <= min(p.list_max, LIST_MAX) &&
+                          r.top_bin >= 0;
+      if (listed) {
+        const double inv = 1.0 / c.temperature;
+        r.slow_x = !(inv < 1e30 && inv > 1e-30);
+        r.inv_t = r.slow_x ? 0.f : float(inv);
+        r.ln_mp = c.min_p > 0 ? float(log(c.min_p)) : -INFINITY;
+        r.mp_tol = c.min_p > 0 ? 1e-6f * (1.f + fabsf(r.ln_mp)) : 0.f;
+        done = K::fast_list(r, c, n_keep, verify, res, p);
+      }
+    }
+    if (r.rank != 0) return;  // rank 0 alone from here; no rank reads another's shared memory any more
+    if (!done) res = K::phase_fp64(r, c);
+    if (threadIdx.x == 0) {
+      if (s.timeout != 0) {
+        res.target_status = ES_INVALID_INPUT;
+        res.status = ES_INVALID_INPUT;
+      }
+      row_results(p.workspace)[r.row] = res;
+      __threadfence();
+      const uint32_t arrived = atomicAdd(&arrivals(p.workspace, p.rows)[c.begin], 1u) + 1;
+      if (arrived == uint32_t(c.end - c.begin)) {
+        __threadfence();
+        finish_request(p, c.req, c.begin, c.end);
+      }
+    }
+    return;
+  }
   if (full_q) r.q_stats_pass();  // the same on every rank
   RowResult res{ES_OK, ES_OK, 0, -1, -1, {0, 0, 0}};
   res.target_status = r.all.bad ? ES_INVALID_INPUT : r.all.valid == 0 ? ES_NO_VALID_TOKEN : ES_OK;

@@ -33,7 +33,28 @@ struct Shards {
   int32_t* status[MAX_SHARDS];
   int32_t* path[MAX_SHARDS];
   const uint64_t* ready[MAX_SHARDS];  // each GPU's "shard written" flag (>= epoch once written)
+  int32_t phases;                   // per-phase mode: every GPU streams only its shard (see PhaseRow)
+  int32_t pad2;
+  uint8_t* exchange[MAX_SHARDS];    // per-phase mode: each GPU's PhaseRow records
+  uint8_t* scratch;                 // per-phase mode: this GPU's FP64 scratch, 16 bytes per token per row
 };
+
+// One row's records in a GPU's exchange buffer (per-phase sharded calls):
+// the GPU-local statistics and tile-maximum bins (from its own top bin
+// down), then the GPU's window candidates (global token IDs), each published
+// with its flag set to the call's epoch (system-scope release).
+constexpr int PHASE_BINS = 128;
+constexpr int PHASE_CAP = 512;
+struct alignas(16) PhaseRow {
+  uint64_t flag_stats, flag_cands;
+  double vmax;
+  int32_t valid, bad, top_bin, n_cand;  // n_cand > PHASE_CAP: this GPU's candidates overflowed
+  uint16_t bins[PHASE_BINS];
+  uint64_t key[PHASE_CAP];
+  int32_t id[PHASE_CAP];
+};
+static_assert(sizeof(PhaseRow) % 16 == 0, "PhaseRow keeps 16-byte alignment");
+static_assert(PHASE_CAP == CAP, "a per-phase record carries one cluster's candidate buffer");
 
 // Kernel arguments (filled by es_verify from es_args); strides in elements.
 struct Params {
@@ -81,6 +102,7 @@ struct Params {
   int32_t stream_rows;     // 0: rows stay in shared memory; else the depth (2..4) of the TMA ring they stream through
   int32_t min_blocks;      // blocks per SM the row kernel's registers must allow (2, or 3 for large streamed batches)
   int32_t fast;            // list rows of at most FAST_KEEP kept tokens may take the warp-level path (es_fast.cuh)
+  int32_t col0, width;     // this call's columns: [col0, col0 + width) of the vocab (col0 > 0 only for a per-phase shard)
   int32_t warm;            // the row kernel has a warm-up warp past its THREADS row threads
   Shards sh;
 };
@@ -90,9 +112,10 @@ struct Outputs {
   int64_t* tokens;
   int32_t *accepted, *status, *path;
 };
-__device__ __forceinline__ int output_sets(const Params& p) { return p.sh.count > 1 ? p.sh.count : 1; }
+__device__ __forceinline__ bool pulls_columns(const Params& p) { return p.sh.count > 1 && !p.sh.phases; }
+__device__ __forceinline__ int output_sets(const Params& p) { return pulls_columns(p) ? p.sh.count : 1; }
 __device__ __forceinline__ Outputs output_set(const Params& p, int i) {
-  if (p.sh.count > 1) return Outputs{p.sh.tokens[i], p.sh.accepted[i], p.sh.status[i], p.sh.path[i]};
+  if (pulls_columns(p)) return Outputs{p.sh.tokens[i], p.sh.accepted[i], p.sh.status[i], p.sh.path[i]};
   return Outputs{p.tokens, p.accepted, p.status, p.path};
 }
 

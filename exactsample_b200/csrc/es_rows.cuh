@@ -215,6 +215,7 @@ template <int DT> struct Row {
   T* slice;          // this rank's logits (resident rows) or the TMA ring (streamed rows)
   const T* tbase;    // the row in global memory (not sharded)
   bool resident, vec, sharded;
+  bool phases;  // a per-phase sharded call: this GPU's columns only, partial results exchanged with the peers
   bool dense;  // after the statistics: no mask and every token of the row valid
   cg::cluster_group cluster;
   int rank, ranks, row, lo, hi, groups;
@@ -237,8 +238,8 @@ template <int DT> struct Row {
     rank = int(cluster.block_rank());
     ranks = int(cluster.num_blocks());
     row = blockIdx.y;
-    lo = min(p.vocab, rank * p.slice_words * 32);
-    hi = min(p.vocab, lo + p.slice_words * 32);
+    lo = min(p.width, rank * p.slice_words * 32);
+    hi = min(p.width, lo + p.slice_words * 32);
     groups = (hi - lo + 3) / 4;
     xc = 0;
     ring_seq = 0;
@@ -246,7 +247,8 @@ template <int DT> struct Row {
     has_mask = p.mask != nullptr;
     resident = !p.stream_rows;
     vec = p.vector_load != 0;
-    sharded = p.sh.count > 1;
+    sharded = pulls_columns(p);
+    phases = p.sh.count > 1 && p.sh.phases;
     dense = false;
     tbase = static_cast<const T*>(p.target) + int64_t(row) * p.t_s0;
   }
@@ -529,6 +531,89 @@ template <int DT> struct Row {
         atomicAdd(&hist_abs[b], uint32_t(__popc(same)));
     }
   }
+  // ---- per-phase sharded calls ----
+  // This row's records in GPU g's exchange buffer.
+  __device__ __forceinline__ PhaseRow* phase_row(int g) const {
+    return reinterpret_cast<PhaseRow*>(p.sh.exchange[g]) + row;
+  }
+  // Thread 0 waits (bounded) until every GPU's flag of this row (statistics
+  // or candidates) holds the call's epoch; block-uniform. A wait that gives
+  // up marks the row on rank 0 (INVALID_INPUT) and counts a timeout.
+  __device__ bool phase_wait(bool cands) {
+    if (threadIdx.x == 0) {
+      int ok = 1;
+      for (int g = 0; g < p.sh.count && ok; ++g) {
+        const uint64_t* f = cands ? &phase_row(g)->flag_cands : &phase_row(g)->flag_stats;
+        for (uint32_t spins = 0; ld_acquire_sys(f) < p.sh.epoch;)
+          if (++spins >= (1u << 20)) {
+            ok = 0;
+            break;
+          }
+      }
+      s.ival[2] = ok;
+      if (!ok) {
+        atomicAdd(&diagnostics(p.workspace, p.rows)->wait_timeouts, 1u);
+        atomicOr(peer(&s.timeout, 0), 1);
+      }
+    }
+    __syncthreads();
+    const bool ok = s.ival[2] != 0;
+    fence_acq_rel_sys();
+    return ok;
+  }
+  // After the statistics merge: rank 0 publishes this GPU's row statistics
+  // and window bins, then every rank merges every GPU's in GPU order, so
+  // that all ranks of all GPUs hold the whole row's values (as the cluster
+  // merge makes them over ranks).
+  __device__ bool phase_stats() {
+    PhaseRow* mine = phase_row(p.sh.rank);
+    if (rank == 0) {
+      if (threadIdx.x == 0) {
+        mine->vmax = double(all.vmax);
+        mine->valid = all.valid;
+        mine->bad = all.bad;
+        mine->top_bin = all.top_bin;
+      }
+      if (int(threadIdx.x) < PHASE_BINS) mine->bins[threadIdx.x] = uint16_t(min(s.win[threadIdx.x], 65535u));
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        __threadfence_system();
+        st_release_sys(&mine->flag_stats, p.sh.epoch);
+      }
+    }
+    if (!phase_wait(false)) return false;
+    if (threadIdx.x == 0) {
+      Stats<W> m{W(-INFINITY), all.qmax, 0, 0, all.qvalid, all.qbad, -1};
+      for (int g = 0; g < p.sh.count; ++g) {
+        PhaseRow* q = phase_row(g);
+        const W v = W(__longlong_as_double(int64_t(ld_relaxed_sys(reinterpret_cast<const uint64_t*>(&q->vmax)))));
+        const int top = int(ld_relaxed_sys(reinterpret_cast<const uint32_t*>(&q->top_bin)));
+        m.vmax = v > m.vmax ? v : m.vmax;
+        m.valid += int(ld_relaxed_sys(reinterpret_cast<const uint32_t*>(&q->valid)));
+        m.bad |= int(ld_relaxed_sys(reinterpret_cast<const uint32_t*>(&q->bad)));
+        m.top_bin = max(m.top_bin, top);
+        s.peer_n[g] = uint32_t(top);
+      }
+      s.in_stats[0] = m;
+    }
+    __syncthreads();
+    all = s.in_stats[0];
+    maxv = all.vmax;
+    top_bin = all.top_bin;
+    dense = !has_mask && all.valid == p.vocab;
+    if (int(threadIdx.x) < PHASE_BINS) {
+      uint32_t n = 0;
+      for (int g = 0; g < p.sh.count; ++g) {
+        const int top = int(s.peer_n[g]);
+        if (top < 0 || int(threadIdx.x) < top_bin - top) continue;
+        n += ld_relaxed_sys(&phase_row(g)->bins[threadIdx.x - (top_bin - top)]);
+      }
+      s.win[threadIdx.x] = n;
+    }
+    __syncthreads();
+    return true;
+  }
+
   // The statistics pass over the whole slice: from shared memory (resident),
   // through the TMA ring (streamed, 16-byte aligned rows), or from global
   // memory; then the cluster merge. Returns false if a copy never arrived.

@@ -2,6 +2,18 @@
 contiguous shards of the vocabulary of every row, as a tensor-parallel LM
 head produces them, and every GPU gets the whole batch's outputs.
 
+Two modes. Per-phase (``phases=True``, the default): every GPU streams only
+its own shard of every row, and the GPUs exchange per-row partial results
+over NVLink, each from the others' exchange buffers behind flags: the row
+statistics with the tile-maximum bins (so every GPU knows the whole row's
+maximum and the candidate window), then the window's candidates, which every
+GPU finishes alike (sort and FP64 finish), writing every request's outputs
+into its own ``plan.out``. Rows this cannot finish (no window, too many
+candidates, or a request off the top-k list path: greedy, full-q drafts,
+masks, lists over 256 tokens) are finished by the independent FP64 path on
+each GPU, reading the whole row from every shard. Column-pulling
+(``phases=False``): the description below.
+
 Each process makes a ``ShardedPlan`` (collectively: the plans exchange the
 handles of their registered buffers), writes its rows' logits shard into
 ``plan.logits[:rows]`` (and the proposal's into ``plan.draft_logits``), and
@@ -95,13 +107,13 @@ class ShardedPlan:
 
     def __init__(self, max_rows: int, max_requests: int, max_draft: int, vocab: int, *, shards: int, rank: int,
                  dtype=None, full_q: bool = False, device: Any = None, group=None,
-                 exchange: Callable[[Any], Sequence] | None = None, connect: bool = True):
+                 exchange: Callable[[Any], Sequence] | None = None, connect: bool = True, phases: bool = True):
         import torch
 
         if not 0 <= rank < shards:
             raise ValueError("rank must be in [0, shards)")
         self.max_rows, self.max_requests, self.max_draft, self.vocab = max_rows, max_requests, max_draft, vocab
-        self.shards, self.rank, self.full_q = shards, rank, full_q
+        self.shards, self.rank, self.full_q, self.phases = shards, rank, full_q, phases
         self.dtype = dtype or torch.float32
         self.cols = shard_columns(vocab, shards)
         self.width = min(self.cols, vocab - rank * self.cols)
@@ -113,7 +125,10 @@ class ShardedPlan:
         # Registered block: flags, shards, outputs (the same layout on every GPU).
         self._layout = layout = {}
         at = 256  # ready flag at 0, done flag at 64, wait timeouts at 128
-        for name, nbytes in [("logits", max_rows * self.cols * item),
+        xbytes = ctypes.c_uint64()
+        capi.check(capi.load().es_shard_exchange_bytes(max_rows, ctypes.byref(xbytes)))
+        for name, nbytes in [("exchange", int(xbytes.value) if phases else 0),
+                             ("logits", max_rows * self.cols * item),
                              ("draft", max_rows * self.cols * item if full_q else 0),
                              ("tokens", max_requests * (max_draft + 1) * 8), ("accepted", max_requests * 4),
                              ("status", max_requests * 4), ("path", max_requests * 4)]:
@@ -139,6 +154,9 @@ class ShardedPlan:
             self._timeouts = _view(self._base + 128, (1,), torch.int32)
             self.workspace = torch.zeros(capi.workspace_bytes(max_rows, vocab, False), dtype=torch.uint8,
                                          device=self.device)
+            # Per-phase mode: the FP64 path's scratch (16 bytes per token per row, this GPU only).
+            self.scratch = (torch.empty(max_rows * vocab * 16, dtype=torch.uint8, device=self.device)
+                            if phases else None)
         if connect:
             self.connect(list((exchange or _all_gather(group))(self.entry)))
 
@@ -197,8 +215,12 @@ class ShardedPlan:
                             list_max=self.list_max if top_k_top_p else 0)
         sh = capi.Shards()
         sh.count, sh.rank, sh.cols, sh.vocab = self.shards, self.rank, self.cols, self.vocab
-        sh.req_begin, sh.req_end = request_range(requests, self.shards, self.rank)
+        sh.req_begin, sh.req_end = (0, requests) if self.phases else request_range(requests, self.shards, self.rank)
         sh.epoch = self.epoch
+        if self.phases:
+            sh.phases = 1
+            sh.exchange = self._ptrs("exchange")
+            sh.scratch = self.scratch.data_ptr()
         for name in ["target", "tokens", "accepted", "status", "path", "ready"]:
             setattr(sh, name, self._ptrs({"target": "logits"}.get(name, name)))
         if self.full_q:

@@ -183,7 +183,26 @@ typedef struct es_shards {
   void* status[ES_MAX_SHARDS];
   void* path[ES_MAX_SHARDS];
   const uint64_t* ready[ES_MAX_SHARDS];  /* every GPU's "shard written" flag */
+  /* Per-phase mode (phases != 0): every GPU reads only its own shard and
+   * finishes every request into its own outputs; the GPUs exchange per-row
+   * partial results (statistics and tile-maximum bins, then the window's
+   * candidates) through each GPU's exchange buffer, es_shard_exchange_bytes
+   * bytes, readable by every GPU. Rows the exchange cannot finish (no
+   * window, too many candidates, or a request outside the top-k list path:
+   * greedy, full-q drafts, masks, lists over 256) are finished by the
+   * independent FP64 path reading the whole row from every shard, with
+   * `scratch` (rows * vocab * 16 bytes of this GPU's memory). req_begin and
+   * req_end must cover every request, and target/draft/ready/tokens/... keep
+   * their meaning (only this GPU's output pointers are written). */
+  int32_t phases;
+  int32_t pad;
+  void* exchange[ES_MAX_SHARDS];
+  void* scratch;
 } es_shards;
+
+/* Bytes of one GPU's exchange buffer for a per-phase sharded call of up to
+ * `rows` target rows. No counterpart in the reference. */
+int es_shard_exchange_bytes(int64_t rows, uint64_t* bytes);
 
 /* es_verify for one GPU of a sharded call: args->target_logits (and
  * draft_logits) are this GPU's shard [rows, its columns]; draft_ids, mask

@@ -42,8 +42,11 @@ def emulated(case, shards, *, dtype=None, calls=1):
     rows, vocab = t["target_logits"].shape
     requests = case["cu_rows"].size - 1
     full_q = t.get("draft_logits") is not None
+    # Column-pulling mode only: per-phase kernels wait on one another, so
+    # they never run as separate launches on one GPU.
     plans = [ShardedPlan(rows, requests, t["_max_draft"], vocab, shards=shards, rank=g,
-                         dtype=t["target_logits"].dtype, full_q=full_q, connect=False) for g in range(shards)]
+                         dtype=t["target_logits"].dtype, full_q=full_q, connect=False, phases=False)
+             for g in range(shards)]
     try:
         entries = [p.entry for p in plans]
         for p in plans:
@@ -69,8 +72,9 @@ def emulated(case, shards, *, dtype=None, calls=1):
             p.close()
 
 
-def distributed(case, group=None, *, dtype=None):
-    """This rank's outputs of a sharded call over the torch.distributed job."""
+def distributed(case, group=None, *, dtype=None, phases=True, calls=1):
+    """This rank's outputs of a sharded call (per-phase or column-pulling)
+    over the torch.distributed job, after `calls` calls on the same plan."""
     import torch
     import torch.distributed as dist
     from exactsample_b200.sharded import ShardedPlan, verify_sharded
@@ -80,10 +84,13 @@ def distributed(case, group=None, *, dtype=None):
     requests = case["cu_rows"].size - 1
     full_q = t.get("draft_logits") is not None
     plan = ShardedPlan(rows, requests, t["_max_draft"], vocab, shards=dist.get_world_size(group),
-                       rank=dist.get_rank(group), dtype=t["target_logits"].dtype, full_q=full_q, group=group)
+                       rank=dist.get_rank(group), dtype=t["target_logits"].dtype, full_q=full_q, group=group,
+                       phases=phases)
     try:
         _fill(plan, t, rows)
-        verify_sharded(plan, rows, t["cu_rows"], t["draft_ids"], **_call_args(t, case))
+        for _ in range(calls):
+            plan.out.tokens.fill_(-777)
+            verify_sharded(plan, rows, t["cu_rows"], t["draft_ids"], **_call_args(t, case))
         torch.cuda.synchronize()
         assert plan.timeouts() == 0
         return _outputs(plan, requests)

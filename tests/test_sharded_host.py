@@ -95,6 +95,38 @@ def test_the_shard_must_be_this_gpus_columns_and_tensors():
     assert code == -1 and "every GPU needs" in text
 
 
+def test_per_phase_tables():
+    """A per-phase call finishes every request on every GPU and needs every
+    GPU's exchange buffer and this GPU's scratch (16-byte aligned)."""
+    def phased(a, **override):
+        sh = _table(a, vocab=24, **override)
+        sh.phases = 1
+        for g in range(2):
+            sh.exchange[g] = a._host.t((64,), np.uint64, capi.ES_U8).data
+        sh.scratch = a._host.t((64,), np.uint64, capi.ES_U8).data
+        return sh
+
+    a = args(rows=2, vocab=16, requests=1)
+    code, message = _call(a, phased(a))
+    assert code == -7, message  # a valid table reaches the device check
+    b = args(rows=2, vocab=16, requests=1)
+    code, text = _call(b, phased(b, req_end=0))
+    assert code == -1 and "every request on every GPU" in text
+    c = args(rows=2, vocab=16, requests=1)
+    sh = phased(c)
+    sh.exchange[1] = None
+    code, text = _call(c, sh)
+    assert code == -1 and "exchange buffer" in text
+    d = args(rows=2, vocab=16, requests=1)
+    sh = phased(d)
+    sh.scratch = None
+    code, text = _call(d, sh)
+    assert code == -1 and "scratch" in text
+    size = ctypes.c_uint64()
+    assert capi.load().es_shard_exchange_bytes(128, ctypes.byref(size)) == 0 and size.value % 16 == 0
+    assert size.value >= 128 * (16 + 8 + 16 + 256 + 512 * 12)
+
+
 def test_flag_and_ipc_entry_points_need_a_gpu():
     lib = capi.load()
     flag = (ctypes.c_uint64 * 1)()
