@@ -109,21 +109,31 @@ def workspace_bytes(rows: int, vocab: int, reference: bool = False) -> int:
     return int(out.value)
 
 
+_CODES: dict = {}
+
+
 def describe(t) -> Tensor:
     """An es_tensor for a torch tensor (None: absent)."""
-    import torch
-
     d = Tensor()
     if t is None:
         return d
-    codes = {torch.float32: ES_F32, torch.float64: ES_F64, torch.float16: ES_F16, torch.bfloat16: ES_BF16,
-             torch.int32: ES_I32, torch.int64: ES_I64, torch.uint8: ES_U8}
-    d.data = t.data_ptr() if t.numel() else None
-    d.dtype = codes.get(t.dtype, -1)
-    d.ndim = t.dim() if 0 < t.dim() <= 2 else -1
-    for i in range(min(t.dim(), 2)):
-        d.size[i] = t.size(i)
-        d.stride[i] = t.stride(i)
+    if not _CODES:
+        import torch
+
+        _CODES.update({torch.float32: ES_F32, torch.float64: ES_F64, torch.float16: ES_F16,
+                       torch.bfloat16: ES_BF16, torch.int32: ES_I32, torch.int64: ES_I64, torch.uint8: ES_U8})
+    if t.numel():
+        d.data = t.data_ptr()
+    d.dtype = _CODES.get(t.dtype, -1)
+    dims = t.dim()
+    if dims == 1:
+        d.ndim, d.size[0], d.stride[0] = 1, t.shape[0], t.stride(0)
+    elif dims == 2:
+        d.ndim = 2
+        d.size[0], d.size[1] = t.shape
+        d.stride[0], d.stride[1] = t.stride()
+    else:
+        d.ndim = -1
     return d
 
 

@@ -369,7 +369,9 @@ template <int DT> struct RowKernel {
       __threadfence_system();
       st_release_sys(&mine->flag_cands, p.sh.epoch);
     }
+    ES_TRACE(p.workspace, p.rows, r.row, r.rank, 19);
     if (!r.phase_wait(true)) return -2;
+    ES_TRACE(p.workspace, p.rows, r.row, r.rank, 20);
     if (threadIdx.x == 0) {
       int total = 0, ok = 1;
       for (int g = 0; g < p.sh.count; ++g) {
@@ -393,6 +395,7 @@ template <int DT> struct RowKernel {
       }
     }
     __syncthreads();
+    ES_TRACE(p.workspace, p.rows, r.row, r.rank, 21);
     return total;
   }
 
@@ -687,6 +690,7 @@ __global__ void __launch_bounds__(THREADS + (WARM ? 32 : 0), MIN_BLOCKS) rows_ke
     }
     if (r.rank != 0) return;  // rank 0 alone from here; no rank reads another's shared memory any more
     if (!done) res = K::phase_fp64(r, c);
+    ES_TRACE(p.workspace, p.rows, r.row, r.rank, 22);
     if (threadIdx.x == 0) {
       if (s.timeout != 0) {
         res.target_status = ES_INVALID_INPUT;

@@ -581,7 +581,9 @@ template <int DT> struct Row {
         st_release_sys(&mine->flag_stats, p.sh.epoch);
       }
     }
+    ES_TRACE(p.workspace, p.rows, row, rank, 16);
     if (!phase_wait(false)) return false;
+    ES_TRACE(p.workspace, p.rows, row, rank, 17);
     if (threadIdx.x == 0) {
       Stats<W> m{W(-INFINITY), all.qmax, 0, 0, all.qvalid, all.qbad, -1};
       for (int g = 0; g < p.sh.count; ++g) {
@@ -611,6 +613,7 @@ template <int DT> struct Row {
       s.win[threadIdx.x] = n;
     }
     __syncthreads();
+    ES_TRACE(p.workspace, p.rows, row, rank, 18);
     return true;
   }
 

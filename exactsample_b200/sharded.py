@@ -142,7 +142,7 @@ class ShardedPlan:
             self._base, self._handle = ptr.value, handle.raw
             _LOCAL_BLOCKS[self._handle] = self._base
             self.entry = (self._handle, os.getpid())
-            self._bases, self._opened = [], []
+            self._bases, self._opened, self._sh = [], [], None
             self.logits = _view(self._base + layout["logits"], (max_rows, self.width), self.dtype, self.cols)
             self.draft_logits = (_view(self._base + layout["draft"], (max_rows, self.width), self.dtype, self.cols)
                                  if full_q else None)
@@ -183,6 +183,24 @@ class ShardedPlan:
             arr[g] = base + self._layout[name] if name in self._layout else base + {"ready": 0, "done": 64}[name]
         return arr
 
+    def _shards(self):
+        """The es_shards of this plan's calls; built once, since the peers'
+        addresses do not change after connect (a call sets the request range
+        and the epoch, and es_verify_sharded reads it only while enqueueing)."""
+        if self._sh is None:
+            sh = capi.Shards()
+            sh.count, sh.rank, sh.cols, sh.vocab = self.shards, self.rank, self.cols, self.vocab
+            if self.phases:
+                sh.phases = 1
+                sh.exchange = self._ptrs("exchange")
+                sh.scratch = self.scratch.data_ptr()
+            for name in ["target", "tokens", "accepted", "status", "path", "ready"]:
+                setattr(sh, name, self._ptrs({"target": "logits"}.get(name, name)))
+            if self.full_q:
+                sh.draft = self._ptrs("draft")
+            self._sh = sh
+        return self._sh
+
     def timeouts(self) -> int:
         """Waits for peer GPUs that gave up so far (synchronizes)."""
         import torch
@@ -213,18 +231,9 @@ class ShardedPlan:
                        accepted_len=self.out.accepted_len, status=self.out.status, path_used=self.out.path_used)
         args = capi.args_of(tensors, mode=_MODES[mode], dispatch=_DISPATCH[dispatch], max_draft=self.max_draft,
                             list_max=self.list_max if top_k_top_p else 0)
-        sh = capi.Shards()
-        sh.count, sh.rank, sh.cols, sh.vocab = self.shards, self.rank, self.cols, self.vocab
+        sh = self._shards()
         sh.req_begin, sh.req_end = (0, requests) if self.phases else request_range(requests, self.shards, self.rank)
         sh.epoch = self.epoch
-        if self.phases:
-            sh.phases = 1
-            sh.exchange = self._ptrs("exchange")
-            sh.scratch = self.scratch.data_ptr()
-        for name in ["target", "tokens", "accepted", "status", "path", "ready"]:
-            setattr(sh, name, self._ptrs({"target": "logits"}.get(name, name)))
-        if self.full_q:
-            sh.draft = self._ptrs("draft")
         capi.check(capi.load().es_verify_sharded(ctypes.byref(args), ctypes.byref(sh), self._stream(stream)))
         self.out.num_requests = requests
 
