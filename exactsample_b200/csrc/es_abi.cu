@@ -112,7 +112,10 @@ __device__ void wait_all(const FlagSet& f) {
 }
 __global__ void wait_flags(const __grid_constant__ FlagSet f) { wait_all(f); }
 // The end of a sharded call on one GPU: its done flag, then every GPU's.
+// Launched as a programmatic dependent of the row kernel, so it first waits
+// for every earlier grid on the stream to complete.
 __global__ void finish_flags(uint64_t* mine, const __grid_constant__ FlagSet f) {
+  wait_for_prerequisite_grid();
   __threadfence_system();
   st_release_sys(mine, f.epoch);
   wait_all(f);
@@ -675,8 +678,17 @@ int es_shard_finish(uint64_t* done, const uint64_t* const* flags, int32_t count,
   f.timeouts = timeouts;
   if (const int dev = device_check(); dev != ES_SUCCESS) return dev;
   cudaGetLastError();
-  es::finish_flags<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(done, f);
-  const cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t config{};
+  config.gridDim = dim3(1);
+  config.blockDim = dim3(1);
+  config.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attr;
+  config.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&config, es::finish_flags, done, f);
+  if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? ES_SUCCESS : fail(ES_ERR_LAUNCH, std::string("finish launch failed: ") + cudaGetErrorString(e));
 }
 

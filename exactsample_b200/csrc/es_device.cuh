@@ -339,6 +339,23 @@ __device__ __forceinline__ uint16_t ld_relaxed_sys(const uint16_t* p) {
   return v;
 }
 __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+// Tagged words of the per-phase exchange: the datum in the low half, the
+// call's tag in the high half, one aligned 64-bit store or load (single-copy
+// atomic), so that the tag vouches for the datum beside it.
+__device__ __forceinline__ void st_tagged_sys(uint64_t* p, uint32_t datum, uint32_t tag) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"((uint64_t(tag) << 32) | datum) : "memory");
+}
+// Polls the word until it carries `tag` (at most `limit` loads); false if it never did.
+__device__ __forceinline__ bool ld_tagged_sys(const uint64_t* p, uint32_t tag, uint32_t& datum, uint32_t limit) {
+  for (uint32_t spins = 0;;) {
+    const uint64_t v = ld_relaxed_sys(p);
+    if (uint32_t(v >> 32) == tag) {
+      datum = uint32_t(v);
+      return true;
+    }
+    if (++spins >= limit) return false;
+  }
+}
 // Programmatic dependent launch: the row kernel starts its loads while the
 // preparation kernel runs, and waits for it before reading what it wrote.
 __device__ __forceinline__ void wait_for_prerequisite_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

@@ -324,7 +324,7 @@ template <int DT> struct RowKernel {
     for (int rr = 0; rr < r.ranks; ++rr) m += s.pushed[rr];
     if (r.phases) {
       if (r.rank != 0) return true;  // rank 0 finishes the row
-      m = phase_candidates(r, m);
+      m = phase_candidates(r, m, n_keep);
       if (m == -2) return true;  // a peer never published: the row is marked invalid
       if (m < 0) return false;   // too many candidates: rank 0 finishes the row in FP64
     } else {
@@ -348,55 +348,73 @@ template <int DT> struct RowKernel {
     return true;
   }
 
-  // Per-phase sharded calls, rank 0 after its cluster's gather: publishes
-  // this GPU's m window candidates (global token IDs) in its exchange
-  // record, waits for every GPU's, and assembles them all in GPU order in
-  // the candidate buffer. Returns their number; -1 when they do not fit
-  // (the row is then finished in FP64, the same decision on every GPU);
-  // -2 when a peer never published.
-  __device__ static int phase_candidates(R& r, int m) {
+  // Per-phase sharded calls, rank 0 after its cluster's gather of m window
+  // candidates: sends this GPU's best into its slot on every GPU, then
+  // assembles every GPU's from its own buffer, in GPU order, in the
+  // candidate buffer. The kept set is the first n_keep of the row's order,
+  // and each of those is among the first n_keep of its own GPU's candidates,
+  // so a GPU sends all m when m <= n_keep, else its first n_keep after a
+  // warp sort (m <= FAST_CAND); more candidates are an overflow. Returns the
+  // number assembled; -1 when a GPU overflowed (the row is then finished in
+  // FP64, the same decision on every GPU); -2 when a GPU's words never arrived.
+  __device__ static int phase_candidates(R& r, int m, int n_keep) {
+    static_assert(FAST_CAND <= PHASE_SEND, "a sorted candidate list fits a slot");
     auto& s = r.s;
     const Params& p = r.p;
-    PhaseRow* mine = r.phase_row(p.sh.rank);
-    const int n = m <= CAP ? m : CAP + 1;
-    for (int i = threadIdx.x; i < min(n, CAP); i += THREADS) {
-      mine->key[i] = s.u.cand.key[i];
-      mine->id[i] = s.u.cand.id[i];
+    const int n = p.sh.count;
+    const uint32_t tag = r.phase_tag();
+    const int send = m > FAST_CAND ? -1 : min(m, n_keep);
+    if (warp_id() == 0) {
+      uint64_t key[2];
+      int32_t id[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int e = lane_id() + 32 * h;
+        key[h] = send >= 0 && e < m ? s.u.cand.key[e] : 0;
+        id[h] = send >= 0 && e < m ? s.u.cand.id[e] : INT_MAX;
+      }
+      if (send >= 0 && send < m) warp_sort<64, sizeof(W) == 8>(key, id);
+      for (int to = 0; to < n; ++to) {
+        uint64_t* slot = r.phase_slot(to, p.sh.rank) + PHASE_COUNT_WORD;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int e = lane_id() + 32 * h;
+          if (e < send) {
+            st_tagged_sys(slot + 1 + 3 * e, uint32_t(key[h]), tag);
+            st_tagged_sys(slot + 2 + 3 * e, uint32_t(key[h] >> 32), tag);
+            st_tagged_sys(slot + 3 + 3 * e, uint32_t(id[h]), tag);
+          }
+        }
+        if (lane_id() == 0) st_tagged_sys(slot, send < 0 ? PHASE_OVERFLOW : uint32_t(send), tag);
+      }
     }
-    if (threadIdx.x == 0) mine->n_cand = n;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence_system();
-      st_release_sys(&mine->flag_cands, p.sh.epoch);
-    }
+    __syncthreads();  // warp 0 is done with the candidate buffer
     ES_TRACE(p.workspace, p.rows, r.row, r.rank, 19);
-    if (!r.phase_wait(true)) return -2;
+    bool ok = true;
+    if (int(threadIdx.x) < n) {
+      uint32_t c = 0;
+      ok = r.phase_read(threadIdx.x, PHASE_COUNT_WORD, c);
+      s.peer_n[threadIdx.x] = c;
+    }
+    if (__syncthreads_or(!ok)) return -2;
     ES_TRACE(p.workspace, p.rows, r.row, r.rank, 20);
-    if (threadIdx.x == 0) {
-      int total = 0, ok = 1;
-      for (int g = 0; g < p.sh.count; ++g) {
-        const int ng = int(ld_relaxed_sys(reinterpret_cast<const uint32_t*>(&r.phase_row(g)->n_cand)));
-        s.pushed[g] = total;
-        s.peer_n[g] = uint32_t(ng);
-        if (ng > CAP) ok = 0;
-        else total += ng;
+    for (int g = 0; g < n; ++g)  // the same on every thread
+      if (s.peer_n[g] == PHASE_OVERFLOW || !r.in_bounds(s.peer_n[g] <= uint32_t(PHASE_SEND), 12)) return -1;
+    int off = 0;
+    for (int g = 0; g < n; ++g) {
+      const int c = int(s.peer_n[g]);
+      for (int i = threadIdx.x; i < 3 * c && ok; i += THREADS) {
+        const int e = i / 3, w = i - 3 * e;
+        uint32_t d = 0;
+        ok = r.phase_read(g, PHASE_COUNT_WORD + 1 + i, d);
+        if (w == 2) s.u.cand.id[off + e] = int32_t(d);
+        else reinterpret_cast<uint32_t*>(&s.u.cand.key[off + e])[w] = d;
       }
-      s.ival[3] = ok && total <= CAP ? total : -1;
+      off += c;
     }
-    __syncthreads();
-    const int total = s.ival[3];
-    if (total < 0) return -1;
-    for (int g = 0; g < p.sh.count; ++g) {
-      const PhaseRow* q = r.phase_row(g);
-      const int ng = int(s.peer_n[g]), off = s.pushed[g];
-      for (int i = threadIdx.x; i < ng; i += THREADS) {
-        s.u.cand.key[off + i] = ld_relaxed_sys(&q->key[i]);
-        s.u.cand.id[off + i] = int32_t(ld_relaxed_sys(reinterpret_cast<const uint32_t*>(&q->id[i])));
-      }
-    }
-    __syncthreads();
+    if (__syncthreads_or(!ok)) return -2;
     ES_TRACE(p.workspace, p.rows, r.row, r.rank, 21);
-    return total;
+    return off;  // <= MAX_SHARDS * PHASE_SEND <= CAP
   }
 
   // Per-phase sharded calls: the whole row in FP64 (es_reference.cuh) by
@@ -409,6 +427,25 @@ template <int DT> struct RowKernel {
     double* w = reinterpret_cast<double*>(p.sh.scratch) + int64_t(r.row) * p.vocab * 2;
     uint64_t* keys = reinterpret_cast<uint64_t*>(w + p.vocab);
     const int row = r.row;
+    // It reads every GPU's shard: each GPU's ready flag (a system-scope
+    // release once its shard is written) first, bounded.
+    if (threadIdx.x == 0) {
+      int ok = 1;
+      for (int g = 0; g < p.sh.count && ok; ++g)
+        for (uint32_t spins = 0; ld_acquire_sys(p.sh.ready[g]) < p.sh.epoch;)
+          if (++spins >= (1u << 20)) {
+            ok = 0;
+            break;
+          }
+      r.s.ival[2] = ok;
+      if (!ok) {
+        atomicAdd(&diagnostics(p.workspace, p.rows)->wait_timeouts, 1u);
+        r.s.timeout = 1;
+      }
+    }
+    __syncthreads();
+    if (r.s.ival[2] == 0) return RowResult{ES_INVALID_INPUT, ES_INVALID_INPUT, 0, -1, -1, {0, 0, 0}};
+    fence_acq_rel_sys();
     return reference_row<THREADS>(
         p, row, c,
         [&](int t) {
@@ -580,6 +617,10 @@ __global__ void __launch_bounds__(THREADS + (WARM ? 32 : 0), MIN_BLOCKS) rows_ke
   T* slice = reinterpret_cast<T*>(raw + smem_slice<DT>(p.slice_words, stream));
   R r(p, s, mask_s, tmax, slice);
   ES_TRACE(p.workspace, p.rows, r.row, r.rank, 0);
+  // A per-phase sharded call's end-of-call flag kernel follows on the
+  // stream as a programmatic dependent: it may be scheduled now, and waits
+  // on the device for this grid's completion.
+  if (r.phases) allow_dependent_grid();
 
   // 1. Start copying this rank's slice (and mask words) before waiting for
   //    the preparation kernel: they are inputs, which it never writes.

@@ -11,8 +11,15 @@ constexpr int CAP = 512;        // candidate buffer of a list row (cluster rank 
 static_assert(CAP >= LIST_MAX, "a list's kept tokens fit the candidate buffer");
 constexpr int DIST_BINS = 128;  // distance-below-maximum bins of 0.5 logit, plus one "far" bin
 constexpr int RADIX = 256;      // digits per radix-select level
-constexpr int MAX_RING_STAGES = 4;     // streamed rows: deepest TMA ring
-constexpr uint32_t RING_CHUNK = 16384; // bytes per ring stage (a multiple of 32 tokens of any dtype)
+#ifndef ES_RING_CHUNK
+#define ES_RING_CHUNK 16384
+#endif
+#ifndef ES_RING_STAGES
+#define ES_RING_STAGES 4
+#endif
+constexpr int MAX_RING_STAGES = ES_RING_STAGES;     // streamed rows: deepest TMA ring
+constexpr uint32_t RING_CHUNK = ES_RING_CHUNK;      // bytes per ring stage
+static_assert(RING_CHUNK % 1024 == 0 && RING_CHUNK <= 16384, "a ring stage holds whole 32-token tiles of any dtype");
 constexpr uint32_t BULK_CHUNK = 16384; // bytes per TMA bulk copy
 
 // Vocabulary-sharded calls: the row's columns live on `count` GPUs, shard g
@@ -35,26 +42,29 @@ struct Shards {
   const uint64_t* ready[MAX_SHARDS];  // each GPU's "shard written" flag (>= epoch once written)
   int32_t phases;                   // per-phase mode: every GPU streams only its shard (see PhaseRow)
   int32_t pad2;
-  uint8_t* exchange[MAX_SHARDS];    // per-phase mode: each GPU's PhaseRow records
+  uint8_t* exchange[MAX_SHARDS];    // per-phase mode: each GPU's PhaseRow inboxes
   uint8_t* scratch;                 // per-phase mode: this GPU's FP64 scratch, 16 bytes per token per row
 };
 
-// One row's records in a GPU's exchange buffer (per-phase sharded calls):
-// the GPU-local statistics and tile-maximum bins (from its own top bin
-// down), then the GPU's window candidates (global token IDs), each published
-// with its flag set to the call's epoch (system-scope release).
+// One row's inbox in a GPU's exchange buffer (per-phase sharded calls): a
+// slot per GPU, which that GPU fills with remote stores, so that every
+// reader polls its own memory. A slot holds the GPU's row statistics and its
+// tile-maximum bins (from its own top bin down), then its best window
+// candidates (global token IDs). Every entry is one 64-bit word: a 32-bit
+// datum below the call's 32-bit tag (the epoch, never 0), stored and loaded
+// whole, so a reader that sees its call's tag in a word also sees that
+// word's datum, with no fence and no separate flag.
 constexpr int PHASE_BINS = 128;
-constexpr int PHASE_CAP = 512;
+constexpr int PHASE_SEND = 64;  // candidates a GPU sends for a row, at most (its first in the order)
+constexpr int PHASE_STAT_WORDS = 4 + PHASE_BINS / 2;  // max (low, high), valid, bad | (top bin + 1) << 1, bins in pairs
+constexpr int PHASE_COUNT_WORD = PHASE_STAT_WORDS;    // candidates sent, or PHASE_OVERFLOW
+constexpr int PHASE_SLOT_WORDS = PHASE_COUNT_WORD + 1 + 3 * PHASE_SEND;  // then key low, key high, ID each
+constexpr uint32_t PHASE_OVERFLOW = 0xffffffffu;
 struct alignas(16) PhaseRow {
-  uint64_t flag_stats, flag_cands;
-  double vmax;
-  int32_t valid, bad, top_bin, n_cand;  // n_cand > PHASE_CAP: this GPU's candidates overflowed
-  uint16_t bins[PHASE_BINS];
-  uint64_t key[PHASE_CAP];
-  int32_t id[PHASE_CAP];
+  uint64_t slot[MAX_SHARDS][PHASE_SLOT_WORDS];
 };
 static_assert(sizeof(PhaseRow) % 16 == 0, "PhaseRow keeps 16-byte alignment");
-static_assert(PHASE_CAP == CAP, "a per-phase record carries one cluster's candidate buffer");
+static_assert(MAX_SHARDS * PHASE_SEND <= CAP, "every GPU's candidates fit the candidate buffer");
 
 // Kernel arguments (filled by es_verify from es_args); strides in elements.
 struct Params {

@@ -146,9 +146,9 @@ template <class W> struct Smem {
   // The statistics exchange's inbox: every rank stores its statistics and
   // tile-maximum bins (from its own top bin down) into every rank's slot
   // before the exchange, so that afterwards each rank reads only its own
-  // shared memory.
+  // shared memory. (Per-phase sharded calls reuse in_win afterwards.)
   Stats<W> in_stats[16];
-  uint16_t in_win[16][WIN_BINS];
+  alignas(16) uint16_t in_win[16][WIN_BINS];
   int32_t pushed[16];  // per-rank counts each rank writes into every rank's copy
   int32_t verdict;     // rank 0's decision on a top-p list, written into every rank's copy
   int32_t tiles[TILE_CAP];
@@ -532,67 +532,65 @@ template <int DT> struct Row {
     }
   }
   // ---- per-phase sharded calls ----
-  // This row's records in GPU g's exchange buffer.
-  __device__ __forceinline__ PhaseRow* phase_row(int g) const {
-    return reinterpret_cast<PhaseRow*>(p.sh.exchange[g]) + row;
+  // GPU g's slot of this row in GPU `to`'s exchange buffer.
+  __device__ __forceinline__ uint64_t* phase_slot(int to, int g) const {
+    return reinterpret_cast<PhaseRow*>(p.sh.exchange[to])[row].slot[g];
   }
-  // Thread 0 waits (bounded) until every GPU's flag of this row (statistics
-  // or candidates) holds the call's epoch; block-uniform. A wait that gives
-  // up marks the row on rank 0 (INVALID_INPUT) and counts a timeout.
-  __device__ bool phase_wait(bool cands) {
-    if (threadIdx.x == 0) {
-      int ok = 1;
-      for (int g = 0; g < p.sh.count && ok; ++g) {
-        const uint64_t* f = cands ? &phase_row(g)->flag_cands : &phase_row(g)->flag_stats;
-        for (uint32_t spins = 0; ld_acquire_sys(f) < p.sh.epoch;)
-          if (++spins >= (1u << 20)) {
-            ok = 0;
-            break;
-          }
-      }
-      s.ival[2] = ok;
-      if (!ok) {
-        atomicAdd(&diagnostics(p.workspace, p.rows)->wait_timeouts, 1u);
-        atomicOr(peer(&s.timeout, 0), 1);
-      }
-    }
-    __syncthreads();
-    const bool ok = s.ival[2] != 0;
-    fence_acq_rel_sys();
-    return ok;
+  // The call's tag: never 0, so a zeroed buffer matches no call.
+  __device__ __forceinline__ uint32_t phase_tag() const { return uint32_t(p.sh.epoch % 0xffffffffull) + 1u; }
+  // Word w of GPU g's slot in this GPU's buffer, once it carries the call's
+  // tag (bounded). A word that never arrives counts a timeout and marks the
+  // row on rank 0; returns false.
+  __device__ bool phase_read(int g, int w, uint32_t& datum) {
+    if (ld_tagged_sys(phase_slot(p.sh.rank, g) + w, phase_tag(), datum, 1u << 20)) return true;
+    atomicAdd(&diagnostics(p.workspace, p.rows)->wait_timeouts, 1u);
+    atomicOr(peer(&s.timeout, 0), 1);
+    return false;
   }
-  // After the statistics merge: rank 0 publishes this GPU's row statistics
-  // and window bins, then every rank merges every GPU's in GPU order, so
-  // that all ranks of all GPUs hold the whole row's values (as the cluster
-  // merge makes them over ranks).
+  // After the statistics merge: rank 0 stores this GPU's row statistics and
+  // window bins into its slot on every GPU; then every rank reads every
+  // GPU's from its own buffer and merges them in GPU order, so that all
+  // ranks of all GPUs hold the whole row's values (as the cluster merge
+  // makes them over ranks). False if a GPU's words never arrived.
   __device__ bool phase_stats() {
-    PhaseRow* mine = phase_row(p.sh.rank);
+    const int n = p.sh.count;
+    const uint32_t tag = phase_tag();
     if (rank == 0) {
-      if (threadIdx.x == 0) {
-        mine->vmax = double(all.vmax);
-        mine->valid = all.valid;
-        mine->bad = all.bad;
-        mine->top_bin = all.top_bin;
-      }
-      if (int(threadIdx.x) < PHASE_BINS) mine->bins[threadIdx.x] = uint16_t(min(s.win[threadIdx.x], 65535u));
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        __threadfence_system();
-        st_release_sys(&mine->flag_stats, p.sh.epoch);
+      const uint64_t vbits = uint64_t(__double_as_longlong(double(all.vmax)));
+      for (int i = threadIdx.x; i < n * PHASE_STAT_WORDS; i += THREADS) {
+        const int to = i / PHASE_STAT_WORDS, w = i - to * PHASE_STAT_WORDS;
+        uint32_t d;
+        if (w == 0) d = uint32_t(vbits);
+        else if (w == 1) d = uint32_t(vbits >> 32);
+        else if (w == 2) d = uint32_t(all.valid);
+        else if (w == 3) d = uint32_t(all.bad != 0) | (uint32_t(all.top_bin + 1) << 1);
+        else d = min(s.win[2 * (w - 4)], 65535u) | (min(s.win[2 * (w - 4) + 1], 65535u) << 16);
+        st_tagged_sys(phase_slot(to, p.sh.rank) + w, d, tag);
       }
     }
     ES_TRACE(p.workspace, p.rows, row, rank, 16);
-    if (!phase_wait(false)) return false;
+    // Every GPU's words, into the cluster-window inbox (free since the
+    // cluster exchange: no rank writes it again in this call).
+    static_assert(sizeof(s.in_win) >= MAX_SHARDS * PHASE_STAT_WORDS * sizeof(uint32_t), "the words fit the inbox");
+    uint32_t* words = reinterpret_cast<uint32_t*>(&s.in_win[0][0]);
+    bool ok = true;
+    for (int i = threadIdx.x; i < n * PHASE_STAT_WORDS; i += THREADS) {
+      const int g = i / PHASE_STAT_WORDS;
+      uint32_t d = 0;
+      if (ok) ok = phase_read(g, i - g * PHASE_STAT_WORDS, d);
+      words[i] = d;
+    }
+    if (__syncthreads_or(!ok)) return false;
     ES_TRACE(p.workspace, p.rows, row, rank, 17);
     if (threadIdx.x == 0) {
       Stats<W> m{W(-INFINITY), all.qmax, 0, 0, all.qvalid, all.qbad, -1};
-      for (int g = 0; g < p.sh.count; ++g) {
-        PhaseRow* q = phase_row(g);
-        const W v = W(__longlong_as_double(int64_t(ld_relaxed_sys(reinterpret_cast<const uint64_t*>(&q->vmax)))));
-        const int top = int(ld_relaxed_sys(reinterpret_cast<const uint32_t*>(&q->top_bin)));
+      for (int g = 0; g < n; ++g) {
+        const uint32_t* q = words + g * PHASE_STAT_WORDS;
+        const W v = W(__longlong_as_double(int64_t((uint64_t(q[1]) << 32) | q[0])));
+        const int top = int(q[3] >> 1) - 1;
         m.vmax = v > m.vmax ? v : m.vmax;
-        m.valid += int(ld_relaxed_sys(reinterpret_cast<const uint32_t*>(&q->valid)));
-        m.bad |= int(ld_relaxed_sys(reinterpret_cast<const uint32_t*>(&q->bad)));
+        m.valid += int(q[2]);
+        m.bad |= int(q[3] & 1u);
         m.top_bin = max(m.top_bin, top);
         s.peer_n[g] = uint32_t(top);
       }
@@ -604,13 +602,12 @@ template <int DT> struct Row {
     top_bin = all.top_bin;
     dense = !has_mask && all.valid == p.vocab;
     if (int(threadIdx.x) < PHASE_BINS) {
-      uint32_t n = 0;
-      for (int g = 0; g < p.sh.count; ++g) {
-        const int top = int(s.peer_n[g]);
-        if (top < 0 || int(threadIdx.x) < top_bin - top) continue;
-        n += ld_relaxed_sys(&phase_row(g)->bins[threadIdx.x - (top_bin - top)]);
+      uint32_t c = 0;
+      for (int g = 0; g < n; ++g) {
+        const int top = int(s.peer_n[g]), b = int(threadIdx.x) - (top_bin - top);  // GPU g's bin index
+        if (top >= 0 && b >= 0) c += (words[g * PHASE_STAT_WORDS + 4 + b / 2] >> (16 * (b & 1))) & 0xffffu;
       }
-      s.win[threadIdx.x] = n;
+      s.win[threadIdx.x] = c;
     }
     __syncthreads();
     ES_TRACE(p.workspace, p.rows, row, rank, 18);

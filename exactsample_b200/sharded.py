@@ -4,15 +4,18 @@ head produces them, and every GPU gets the whole batch's outputs.
 
 Two modes. Per-phase (``phases=True``, the default): every GPU streams only
 its own shard of every row, and the GPUs exchange per-row partial results
-over NVLink, each from the others' exchange buffers behind flags: the row
+over NVLink. Each GPU stores its results into its slot in every GPU's
+exchange buffer, as 64-bit words that carry the call's tag beside each
+datum, and reads the others' from its own buffer. They are the row
 statistics with the tile-maximum bins (so every GPU knows the whole row's
-maximum and the candidate window), then the window's candidates, which every
-GPU finishes alike (sort and FP64 finish), writing every request's outputs
-into its own ``plan.out``. Rows this cannot finish (no window, too many
-candidates, or a request off the top-k list path: greedy, full-q drafts,
-masks, lists over 256 tokens) are finished by the independent FP64 path on
-each GPU, reading the whole row from every shard. Column-pulling
-(``phases=False``): the description below.
+maximum and the candidate window), then each GPU's best window candidates
+(at most the top-k), which every GPU finishes alike (sort and FP64 finish),
+writing every request's outputs into its own ``plan.out``. Rows this cannot
+finish (no window, more than 64 candidates on a GPU that must cut them, or
+a request off the top-k list path: greedy, full-q drafts, masks, lists over
+256 tokens) are finished by the independent FP64 path on each GPU, reading
+the whole row from every shard. Column-pulling (``phases=False``): the
+description below.
 
 Each process makes a ``ShardedPlan`` (collectively: the plans exchange the
 handles of their registered buffers), writes its rows' logits shard into

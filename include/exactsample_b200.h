@@ -185,15 +185,17 @@ typedef struct es_shards {
   const uint64_t* ready[ES_MAX_SHARDS];  /* every GPU's "shard written" flag */
   /* Per-phase mode (phases != 0): every GPU reads only its own shard and
    * finishes every request into its own outputs; the GPUs exchange per-row
-   * partial results (statistics and tile-maximum bins, then the window's
-   * candidates) through each GPU's exchange buffer, es_shard_exchange_bytes
-   * bytes, readable by every GPU. Rows the exchange cannot finish (no
-   * window, too many candidates, or a request outside the top-k list path:
-   * greedy, full-q drafts, masks, lists over 256) are finished by the
-   * independent FP64 path reading the whole row from every shard, with
-   * `scratch` (rows * vocab * 16 bytes of this GPU's memory). req_begin and
-   * req_end must cover every request, and target/draft/ready/tokens/... keep
-   * their meaning (only this GPU's output pointers are written). */
+   * partial results (statistics and tile-maximum bins, then each GPU's best
+   * window candidates): each GPU stores its own into every GPU's exchange
+   * buffer (es_shard_exchange_bytes bytes, zeroed when allocated, writable
+   * by every GPU) and reads the others' from its own. Rows the exchange
+   * cannot finish (no window, more than 64 candidates on a GPU that must cut
+   * them, or a request outside the top-k list path: greedy, full-q drafts,
+   * masks, lists over 256) are finished by the independent FP64 path
+   * reading the whole row from every shard, with `scratch` (rows * vocab *
+   * 16 bytes of this GPU's memory). req_begin and req_end must cover every
+   * request, and target/draft/ready/tokens/... keep their meaning (only this
+   * GPU's output pointers are written). */
   int32_t phases;
   int32_t pad;
   void* exchange[ES_MAX_SHARDS];
