@@ -30,7 +30,8 @@ NVCC = str(CUDA_HOME / "bin" / "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [*ARCH, "-O3", "-std=c++17", "--fmad=false", "-lineinfo", "-Xcompiler", "-fPIC",
               "-Xptxas", "-warn-spills", f"-I{INCLUDE}"]
-CUDA_SOURCES = ["es_abi.cu", "es_rows_f32.cu", "es_rows_f64.cu", "es_rows_f16.cu", "es_rows_bf16.cu"]
+CUDA_SOURCES = ["es_abi.cu", "es_rows_f32.cu", "es_rows_f64.cu", "es_rows_f16.cu", "es_rows_bf16.cu",
+                "es_rows_full_f32.cu", "es_rows_full_f64.cu", "es_rows_full_f16.cu", "es_rows_full_bf16.cu"]
 HEADERS = sorted(CSRC.glob("*.cuh")) + [INCLUDE / "exactsample_b200.h"]
 
 CORE_LIB = PACKAGE / "libexactsample_b200.so"

@@ -98,6 +98,7 @@ __global__ void signal_flag(uint64_t* flag, uint64_t epoch) {
 struct FlagSet {
   const uint64_t* flag[MAX_SHARDS];
   int32_t count;
+  int32_t rank;  // finish_flags: this GPU's slot in every GPU's array
   uint64_t epoch;
   uint32_t* timeouts;
 };
@@ -111,14 +112,23 @@ __device__ void wait_all(const FlagSet& f) {
   __threadfence_system();
 }
 __global__ void wait_flags(const __grid_constant__ FlagSet f) { wait_all(f); }
-// The end of a sharded call on one GPU: its done flag, then every GPU's.
-// Launched as a programmatic dependent of the row kernel, so it first waits
-// for every earlier grid on the stream to complete.
+// The end of a sharded call on one GPU, one thread per GPU g: this GPU's tag
+// into its slot of GPU g's array (a remote system-scope release), then GPU
+// g's tag from this GPU's own array (local polls). Launched as a programmatic
+// dependent of the row kernel, so it first waits for every earlier grid on
+// the stream to complete.
 __global__ void finish_flags(uint64_t* mine, const __grid_constant__ FlagSet f) {
   wait_for_prerequisite_grid();
+  const int g = threadIdx.x;
+  if (g >= f.count) return;
   __threadfence_system();
-  st_release_sys(mine, f.epoch);
-  wait_all(f);
+  st_release_sys(const_cast<uint64_t*>(f.flag[g]) + f.rank, f.epoch);
+  for (uint32_t spins = 0; ld_acquire_sys(mine + g) < f.epoch;)
+    if (++spins >= (1u << 20)) {
+      if (f.timeouts != nullptr) atomicAdd(f.timeouts, 1u);
+      break;
+    }
+  __threadfence_system();
 }
 
 template <int DT> cudaError_t launch_rows(const Params& p, int cluster, cudaStream_t stream);
@@ -500,8 +510,11 @@ int verify_impl(const es_args* a, cudaStream_t stream, cudaEvent_t before, cudaE
                              &p.min_blocks);
     if (cluster < 0) return fail(ES_ERR_UNSUPPORTED, "vocabulary too large for one 16-block cluster's shared memory");
     // The warm-up warp pays off where rows are split over ranks (one rank
-    // per row leaves the chain after the statistics a smaller share).
-    if (cluster < 2) p.warm = 0;
+    // per row leaves the chain after the statistics a smaller share) and
+    // streamed: its dry run (about 20 us of cold instruction fetch) hides
+    // behind a stream of 20 us or more, but would hold back the first
+    // cluster exchange of resident rows, whose statistics take a few us.
+    if (cluster < 2 || p.stream_rows == 0) p.warm = 0;
     const size_t e = element_size(logits.dtype);
     p.vector_load = logits.stride[1] == 1 && reinterpret_cast<uintptr_t>(logits.data) % 16 == 0 &&
                     (uint64_t(logits.stride[0]) * e) % 16 == 0;  // always so for shards (checked above)
@@ -667,12 +680,15 @@ int es_shard_finish(uint64_t* done, const uint64_t* const* flags, int32_t count,
                     void* stream) {
   g_error.clear();
   if (done == nullptr || flags == nullptr || count < 1 || count > es::MAX_SHARDS)
-    return fail(ES_ERR_ARGUMENT, "flags: this GPU's done flag and 1 to 8 flags");
+    return fail(ES_ERR_ARGUMENT, "flags: this GPU's slot array and 1 to 8 slot arrays");
   es::FlagSet f{};
+  f.rank = -1;
   for (int g = 0; g < count; ++g) {
     if (flags[g] == nullptr) return fail(ES_ERR_ARGUMENT, "null flag");
     f.flag[g] = flags[g];
+    if (flags[g] == done) f.rank = g;
   }
+  if (f.rank < 0) return fail(ES_ERR_ARGUMENT, "this GPU's slot array must be one of the slot arrays");
   f.count = count;
   f.epoch = epoch;
   f.timeouts = timeouts;
@@ -680,7 +696,7 @@ int es_shard_finish(uint64_t* done, const uint64_t* const* flags, int32_t count,
   cudaGetLastError();
   cudaLaunchConfig_t config{};
   config.gridDim = dim3(1);
-  config.blockDim = dim3(1);
+  config.blockDim = dim3(32);
   config.stream = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

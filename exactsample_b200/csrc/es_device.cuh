@@ -48,6 +48,36 @@ __device__ __forceinline__ Words philox(uint32_t c0, uint32_t c1, uint32_t c2, u
   return Words{{c0, c1, c2, c3}};
 }
 
+// The words of every group of one row and substream. Only the counter's
+// last word (the group) varies, and it enters round 1 by one XOR into the
+// third word; round 2's first product does not depend on it. So round 1 and
+// half of round 2 are computed once: with a2 = round 1's third word before
+// the XOR, b0 = the XOR terms of round 2's first word, b2 and b3 = round 2's
+// third and fourth words, and (k0, k1) = round 3's key, a group's words are
+// round 2's remaining product and 8 full rounds (the same 10-round
+// Philox4x32 as philox()).
+constexpr uint32_t PHILOX_M0 = 0xD2511F53u, PHILOX_M1 = 0xCD9E8D57u;
+constexpr uint32_t PHILOX_W0 = 0x9E3779B9u, PHILOX_W1 = 0xBB67AE85u;
+struct PhiloxRow {
+  uint32_t a2, b0, b2, b3, k0, k1;
+  __device__ __forceinline__ Words group(uint32_t g) const {
+    const uint32_t x = a2 ^ g;
+    uint32_t c0 = __umulhi(x, PHILOX_M1) ^ b0, c1 = x * PHILOX_M1, c2 = b2, c3 = b3, key0 = k0, key1 = k1;
+#pragma unroll
+    for (int round = 2; round < 10; ++round) {
+      const uint32_t lo0 = c0 * PHILOX_M0, hi0 = __umulhi(c0, PHILOX_M0);
+      const uint32_t lo1 = c2 * PHILOX_M1, hi1 = __umulhi(c2, PHILOX_M1);
+      c0 = hi1 ^ c1 ^ key0;
+      c1 = lo1;
+      c2 = hi0 ^ c3 ^ key1;
+      c3 = lo0;
+      key0 += PHILOX_W0;
+      key1 += PHILOX_W1;
+    }
+    return Words{{c0, c1, c2, c3}};
+  }
+};
+
 // One request row's RNG address without the substream and token.
 struct Address {
   uint32_t stream, position, k0, k1;
@@ -56,6 +86,22 @@ struct Address {
   }
   __device__ __forceinline__ uint32_t word(uint32_t substream, uint32_t token) const {
     return group(substream, token >> 2).w[token & 3];
+  }
+  // Counter (stream, position, substream, g) for every group g: rounds 1
+  // and 2 as far as they do not depend on g (PhiloxRow).
+  __device__ __forceinline__ PhiloxRow row(uint32_t substream) const {
+    const uint32_t a0 = __umulhi(substream, PHILOX_M1) ^ position ^ k0;  // round 1's first word
+    const uint32_t a1 = substream * PHILOX_M1;                            // its second
+    const uint32_t a3 = stream * PHILOX_M0;                               // its fourth
+    const uint32_t k0b = k0 + PHILOX_W0, k1b = k1 + PHILOX_W1;            // round 2's key
+    PhiloxRow r;
+    r.a2 = __umulhi(stream, PHILOX_M0) ^ k1;
+    r.b0 = a1 ^ k0b;
+    r.b2 = __umulhi(a0, PHILOX_M0) ^ a3 ^ k1b;
+    r.b3 = a0 * PHILOX_M0;
+    r.k0 = k0b + PHILOX_W0;
+    r.k1 = k1b + PHILOX_W1;
+    return r;
   }
 };
 

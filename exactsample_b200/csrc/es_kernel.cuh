@@ -559,6 +559,59 @@ template <int DT> struct RowKernel {
     res.residual = full_q ? r.draw_residual_q(kept, sp, sq) : r.draw(2, x, kept, cuts, p.exact_draws != 0);
     return false;
   }
+
+  // positive() for kernels compiled without the list paths (calls with
+  // list_max = 0): the cuts, the ratio test and the draws over the full row,
+  // with the group-screened draw.
+  __device__ __forceinline__ static bool positive_rows(R& r, const RowCtx& c, bool verify, bool full_q, double sq,
+                                                       RowResult& res, const Params& p) {
+    const int valid = r.all.valid;
+    const int64_t k = c.top_k;
+    const int n_keep = (k > 0 && k < valid) ? int(k) : valid;
+    Cut<Key> cut_k{0, 0, 0}, cut_p{0, 0, 0};
+    if (k > 0 && k < valid) cut_k = r.select_nth(int(k), [](Key, int, W) { return true; });
+    ES_TRACE(p.workspace, p.rows, r.row, r.rank, 4);
+    double sp = 0;
+    bool sp_known = false;
+    if (r.top_p < 1) {
+      cut_p = r.top_p_cut(cut_k, &sp);
+      sp_known = true;
+    }
+    ES_TRACE(p.workspace, p.rows, r.row, r.rank, 5);
+    auto kept = [cut_k, cut_p](Key key, int t) { return cut_k.keeps(key, t) && cut_p.keeps(key, t); };
+    const bool cuts = cut_k.on || cut_p.on;
+    if (!verify) {
+      res.sample = r.draw_groups(0, -1, kept, cuts, p.exact_draws != 0);
+      ES_TRACE(p.workspace, p.rows, r.row, r.rank, 12);
+      return false;
+    }
+    const int x = c.draft_id;
+    double wx = 0;  // the draft token's weight, if kept
+    if (r.valid_global(x)) {
+      const W v = r.value_global(x);
+      if (kept(order_key(v), x)) {
+        const double w = exp(r.x64(v));
+        if (w >= r.min_p && w > 0) wx = w;
+      }
+    }
+    const double qx = q_of_draft(r, c, full_q, sq);
+    const double u = uniform64(r.addr.word(1, 0));
+    // The oracle's test u < min(1, (wx / sp) / qx) falls as sp grows (every
+    // step rounds monotonically), so bounds on sp usually settle it without
+    // the exact sum, which one-hot residual draws do not need either.
+    int accept = wx == 0 ? 0 : -1;
+    if (accept < 0 && !sp_known && !p.exact_draws) {
+      const Interval m = r.approx_mass(kept, cuts);
+      if (u < fmin(1.0, (wx / m.hi) / qx)) accept = 1;
+      else if (m.lo > 0 && !(u < fmin(1.0, (wx / m.lo) / qx))) accept = 0;
+    }
+    if (!sp_known && (accept < 0 || (accept == 0 && full_q))) sp = r.exact_mass(kept);
+    if (accept < 0) accept = u < fmin(1.0, (wx / sp) / qx);
+    res.accept = accept != 0;
+    if (res.accept) return false;
+    res.residual = full_q ? r.draw_residual_q(kept, sp, sq) : r.draw_groups(2, x, kept, cuts, p.exact_draws != 0);
+    return false;
+  }
 };
 
 // The warm-up warp (es_fast.cuh): the warp-level list steps once on dummy
@@ -602,9 +655,12 @@ template <int DT> __device__ void warm_up(Smem<typename Types<DT>::W>& s) {
 
 // MIN_BLOCKS: resident CTAs per SM the register allocation must allow (3 for
 // large streamed batches, else 2). Blocks have THREADS row threads, plus a
-// warm-up warp with WARM (p.warm).
-template <int DT, int MIN_BLOCKS, bool WARM>
+// warm-up warp with WARM (p.warm). LISTS: the list paths are compiled in
+// (calls with list_max > 0); without them the kernel is smaller and its
+// full-row draws screen whole groups first.
+template <int DT, int MIN_BLOCKS, bool WARM, bool LISTS>
 __global__ void __launch_bounds__(THREADS + (WARM ? 32 : 0), MIN_BLOCKS) rows_kernel(const __grid_constant__ Params p) {
+  static_assert(LISTS || !WARM, "the warm-up warp runs the list path");
   using K = RowKernel<DT>;
   using R = typename K::R;
   using T = typename K::T;
@@ -774,7 +830,8 @@ __global__ void __launch_bounds__(THREADS + (WARM ? 32 : 0), MIN_BLOCKS) rows_ke
       r.inv_t = r.slow_x ? 0.f : float(inv);
       r.ln_mp = c.min_p > 0 ? float(log(c.min_p)) : -INFINITY;
       r.mp_tol = c.min_p > 0 ? 1e-6f * (1.f + fabsf(r.ln_mp)) : 0.f;
-      solo = K::positive(r, c, verify, full_q, sq, res, p);
+      if constexpr (LISTS) solo = K::positive(r, c, verify, full_q, sq, res, p);
+      else solo = K::positive_rows(r, c, verify, full_q, sq, res, p);
     }
   }
 
@@ -799,10 +856,16 @@ __global__ void __launch_bounds__(THREADS + (WARM ? 32 : 0), MIN_BLOCKS) rows_ke
 
 // Launch of the row kernel: a (C, rows) grid of C-block clusters, with
 // programmatic stream serialization after the preparation kernel.
-template <int DT> cudaError_t launch_rows(const Params& p, int cluster, cudaStream_t stream) {
+// One kernel family's launch: LISTS picks the kernels compiled with the
+// list paths (calls with list_max > 0) or without them.
+template <int DT, bool LISTS> cudaError_t launch_family(const Params& p, int cluster, cudaStream_t stream) {
   const size_t smem = smem_bytes<DT>(p.slice_words, p.stream_rows);
-  auto kernel = p.min_blocks == 3 ? (p.warm ? rows_kernel<DT, 3, true> : rows_kernel<DT, 3, false>)
-                                  : (p.warm ? rows_kernel<DT, 2, true> : rows_kernel<DT, 2, false>);
+  void (*kernel)(Params);
+  if constexpr (LISTS)
+    kernel = p.min_blocks == 3 ? (p.warm ? rows_kernel<DT, 3, true, true> : rows_kernel<DT, 3, false, true>)
+                               : (p.warm ? rows_kernel<DT, 2, true, true> : rows_kernel<DT, 2, false, true>);
+  else
+    kernel = p.min_blocks == 3 ? rows_kernel<DT, 3, false, false> : rows_kernel<DT, 2, false, false>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   if (cluster > 8) {
@@ -824,6 +887,21 @@ template <int DT> cudaError_t launch_rows(const Params& p, int cluster, cudaStre
   config.attrs = attrs;
   config.numAttrs = 2;
   return cudaLaunchKernelEx(&config, kernel, p);
+}
+
+// Calls without lists launch kernels compiled in translation units of their
+// own (es_rows_full_*.cu): the compiler's inlining and register allocation
+// depend on everything a translation unit holds, and apart the list kernels
+// compile as they do alone.
+template <int DT> cudaError_t launch_rows_full(const Params& p, int cluster, cudaStream_t stream);
+template <> cudaError_t launch_rows_full<ES_F32>(const Params&, int, cudaStream_t);
+template <> cudaError_t launch_rows_full<ES_F64>(const Params&, int, cudaStream_t);
+template <> cudaError_t launch_rows_full<ES_F16>(const Params&, int, cudaStream_t);
+template <> cudaError_t launch_rows_full<ES_BF16>(const Params&, int, cudaStream_t);
+
+template <int DT> cudaError_t launch_rows(const Params& p, int cluster, cudaStream_t stream) {
+  if (p.list_max == 0) return launch_rows_full<DT>(p, cluster, stream);
+  return launch_family<DT, true>(p, cluster, stream);
 }
 
 // Launch of the independent FP64 kernel (dispatch="reference"): one block per row.

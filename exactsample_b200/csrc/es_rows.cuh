@@ -1554,6 +1554,189 @@ template <int DT> struct Row {
 
   // The residual draw max(p - q, 0) of a full-q draft row over the kept set,
   // in FP64 exactly as the oracle forms it: p = w / Sp, q = wq / Sq.
+  // draw() for kernels compiled without the list paths: every group of four
+  // tokens is screened whole before its tokens are, and the Philox words come
+  // from the row's precomputed rounds. Same result as draw().
+  template <class Kept> __device__ int draw_groups(uint32_t sub, int excluded, Kept kept, bool cuts, bool exact_only) {
+    // A kept token's score bounds the winner's from below: the maximum
+    // (x = 0), unless it is excluded.
+    const int greedy = argmax_id();
+    if (threadIdx.x == 0) {
+      float floor = -INFINITY;
+      const int t = greedy != excluded ? greedy : INT_MAX;
+      if (t != INT_MAX && valid_global(t)) {
+        const W v = value_global(t);
+        const float x = x32(v);
+        if (kept(order_key(v), t) && weight_kept(v, x)) {
+          const float g = noise32(addr.word(sub, uint32_t(t)));
+          const float sc = __fadd_rn(x, g);
+          floor = __fsub_rn(sc, 1.01f * SCORE_ERR * (1.f + fabsf(x) + fabsf(g)));
+        }
+      }
+      s.floor_score = floor;
+    }
+    __syncthreads();
+    const float floor = exact_only ? -INFINITY : s.floor_score;
+    Pick best = no_pick();
+    float skipped = -INFINITY;
+    if (!exact_only) {
+      // Screens, from cheap to exact, against bar = the best lower bound so
+      // far (or the floor) less PRUNE_MARGIN. A token screened out has an
+      // upper bound below the bar, so `skipped` takes the bar itself: below
+      // the winner's lower bound by the margin, it never blocks the
+      // certificate. The screens' own FP32 roundings (about 1e-5) are
+      // covered by slacks of 1e-3 and 1e-4.
+      //
+      // `bar` follows best.lo (it only rises); x_live is the value screen's
+      // threshold for it: x + NOISE_MAX + SCORE_ERR (1 + |x| + NOISE_MAX) < bar,
+      // i.e. (x <= 0) x < (bar - LIVE_OFFSET) / (1 - SCORE_ERR).
+      float bar = 0.f, x_live = 0.f;
+      auto raise_bar = [&]() {
+        bar = fmaxf(floor, best.lo) - PRUNE_MARGIN;
+        x_live = __fsub_rn(__fmul_rn(__fsub_rn(bar, LIVE_OFFSET), 1.f + 2.f * SCORE_ERR), 1e-3f);
+      };
+      raise_bar();
+      // Noise, integers only: G(w) <= (clz(~w) + 1) ln 2, since
+      // -log(u) >= 1 - u >= 2^-(clz(~w) + 1); the bound rises with x and with
+      // the word.
+      auto cheap_ub = [](float x, int l) {
+        const float gn = __fmul_rn(float(l + 1), LN2_UP);
+        return __fadd_rn(__fadd_rn(__fmul_rn(x, 1.f - SCORE_ERR), __fmul_rn(gn, 1.f + SCORE_ERR)), SCORE_ERR + 1e-4f);
+      };
+      const PhiloxRow ph = addr.row(sub);
+      slice_pass([&](int g, const W* v, unsigned bits) {
+        if (!bits) return;
+        float xs[4];
+        unsigned live = 0;
+        Words r;
+        if (!cuts) {
+          // Every valid token is a candidate: the group is screened whole,
+          // with one x (x32 is monotone, so the largest valid value has the
+          // largest x) and one noise bound (the largest of the four words
+          // has the largest).
+          W vm = W(-INFINITY);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if ((bits >> j) & 1u) vm = v[j] > vm ? v[j] : vm;
+          const float xg = x32(vm);
+          if (xg < x_live) {
+            skipped = fmaxf(skipped, bar);
+            return;
+          }
+          r = ph.group(uint32_t((lo >> 2) + g));
+          const uint32_t wm = max(max(r.w[0], r.w[1]), max(r.w[2], r.w[3]));
+          if (cheap_ub(xg, __clz(~wm)) < bar) {
+            skipped = fmaxf(skipped, bar);
+            return;
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            xs[j] = x32(v[j]);
+            if (((bits >> j) & 1u) && xs[j] >= x_live) live |= 1u << j;
+          }
+        } else {
+          // A cut rejects most tokens: membership first, so that the
+          // rejected ones need no Philox words.
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            xs[j] = x32(v[j]);
+            if (((bits >> j) & 1u) && xs[j] >= x_live && kept(order_key(v[j]), lo + 4 * g + j)) live |= 1u << j;
+          }
+          if (live != bits) skipped = fmaxf(skipped, bar);
+          if (!live) return;
+          r = ph.group(uint32_t((lo >> 2) + g));
+          int lmax = 0;
+          float xmax = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if ((live >> j) & 1u) {
+              lmax = max(lmax, int(__clz(~r.w[j])));
+              xmax = fmaxf(xmax, xs[j]);
+            }
+          if (cheap_ub(xmax, lmax) < bar) {
+            skipped = fmaxf(skipped, bar);
+            return;
+          }
+        }
+        if (live != bits) skipped = fmaxf(skipped, bar);
+        // The per-token screens of the live tokens.
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (!((live >> j) & 1u)) continue;
+          const float x = xs[j];
+          if (cheap_ub(x, __clz(~r.w[j])) < bar) {
+            skipped = fmaxf(skipped, bar);
+            continue;
+          }
+          // The rare token that might still win: exact membership, a
+          // tighter noise bound, then the certified FP32 score.
+          const int t = lo + 4 * g + j;
+          if (t == excluded || (!cuts && !kept(order_key(v[j]), t)) || !weight_kept(v[j], x)) continue;
+          const float gu = noise_upper(r.w[j]);
+          const float ub = x + gu + SCORE_ERR * (1.f + fabsf(x) + fabsf(gu));
+          if (ub < bar) {
+            skipped = fmaxf(skipped, ub);
+            continue;
+          }
+          const float G = noise32(r.w[j]);
+          const float sc = __fadd_rn(x, G);
+          const float err = SCORE_ERR * (1.f + fabsf(x) + fabsf(G));
+          best = pick_of(best, Pick{sc, sc - err, sc + err, -INFINITY, t});
+          raise_bar();
+        }
+      });
+    }
+    ES_TRACE(p.workspace, p.rows, row, rank, 13);
+    best.others = fmaxf(best.others, skipped);
+    best = block_all(best, [](Pick a, Pick b) { return pick_of(a, b); }, s.red.picks);
+    if (threadIdx.x == 0) s.pick[parity()] = best;
+    exchange();
+    if (int(threadIdx.x) < ranks) s.peers.picks[threadIdx.x] = *peer(&s.pick[parity() ^ 1], threadIdx.x);
+    __syncthreads();
+    Pick top = no_pick();
+    for (int r = 0; r < ranks; ++r) top = pick_of(top, s.peers.picks[r]);
+    __syncthreads();
+    if (!exact_only) {
+      if (top.id == INT_MAX) return -1;
+      if (top.lo > top.others) return top.id;
+      count_fallback();
+    }
+    ES_TRACE(p.workspace, p.rows, row, rank, 14);
+    // FP64: every kept token whose upper bound reaches the threshold.
+    const float threshold = exact_only ? -INFINITY : top.lo;
+    Best b = no_best();
+    for (int g = threadIdx.x; g < groups; g += THREADS) {
+      W v[4];
+      const unsigned bits = group(g, v);
+      unsigned live = 0;
+      float xs[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int t = lo + 4 * g + j;
+        xs[j] = 0.f;
+        if (!((bits >> j) & 1u) || t == excluded) continue;
+        const float x = x32(v[j]);
+        if (!kept(order_key(v[j]), t) || !weight_kept(v[j], x)) continue;
+        xs[j] = x;
+        if (exact_only || x + NOISE_MAX + SCORE_ERR * (1.f + fabsf(x) + NOISE_MAX) >= threshold) live |= 1u << j;
+      }
+      if (!live) continue;
+      const Words r = addr.group(sub, uint32_t((lo >> 2) + g));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (!((live >> j) & 1u)) continue;
+        if (!exact_only) {
+          const float gu = noise_upper(r.w[j]);
+          if (xs[j] + gu + SCORE_ERR * (1.f + fabsf(xs[j]) + fabsf(gu)) < threshold) continue;
+        }
+        b = best_of(b, Best{x64(v[j]) + noise64(r.w[j]), lo + 4 * g + j});
+      }
+    }
+    return cluster_best(b);
+  }
+
+  // The residual draw max(p - q, 0) of a full-q draft row over the kept set,
+  // in FP64 exactly as the oracle forms it: p = w / Sp, q = wq / Sq.
   template <class Kept> __device__ int draw_residual_q(Kept kept, double sp, double sq) {
     Best b = no_best();
     for (int g = threadIdx.x; g < groups; g += THREADS) {

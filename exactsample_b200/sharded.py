@@ -127,7 +127,7 @@ class ShardedPlan:
         item = torch.empty((), dtype=self.dtype).element_size()
         # Registered block: flags, shards, outputs (the same layout on every GPU).
         self._layout = layout = {}
-        at = 256  # ready flag at 0, done flag at 64, wait timeouts at 128
+        at = 256  # ready flag at 0, done flag at 64, wait timeouts at 128, done slots (one per GPU) at 192
         xbytes = ctypes.c_uint64()
         capi.check(capi.load().es_shard_exchange_bytes(max_rows, ctypes.byref(xbytes)))
         for name, nbytes in [("exchange", int(xbytes.value) if phases else 0),
@@ -183,7 +183,7 @@ class ShardedPlan:
     def _ptrs(self, name: str):
         arr = (ctypes.c_void_p * capi.MAX_SHARDS)()
         for g, base in enumerate(self._bases):
-            arr[g] = base + self._layout[name] if name in self._layout else base + {"ready": 0, "done": 64}[name]
+            arr[g] = base + self._layout[name] if name in self._layout else base + {"ready": 0, "done": 64, "slots": 192}[name]
         return arr
 
     def _shards(self):
@@ -249,9 +249,10 @@ class ShardedPlan:
                                              self.epoch, ctypes.c_void_p(self._base + 128), self._stream(stream)))
 
     def finish(self, stream=None) -> None:
-        """signal_done and wait_done as one launch."""
-        flags = self._ptrs("done")
-        capi.check(capi.load().es_shard_finish(ctypes.c_void_p(self._base + 64),
+        """The end of a call: this GPU's tag into its slot on every GPU, then
+        every GPU's tag in this GPU's slots (one launch)."""
+        flags = self._ptrs("slots")
+        capi.check(capi.load().es_shard_finish(ctypes.c_void_p(self._base + 192),
                                                ctypes.cast(flags, ctypes.POINTER(ctypes.c_void_p)), self.shards,
                                                self.epoch, ctypes.c_void_p(self._base + 128), self._stream(stream)))
 

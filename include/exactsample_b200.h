@@ -155,15 +155,22 @@ int es_verify_static(const es_args* args, void* stream);
  *   es_verify_sharded(args, shards)        raises this GPU's ready flag, and
  *                                          waits for every GPU's before
  *                                          reading a shard;
- *   es_shard_finish(done[rank], done, count, epoch)
- *                                          raises this GPU's done flag and
- *                                          waits for every GPU's: afterwards
- *                                          every GPU's outputs are complete
- *                                          and no GPU reads this GPU's shard.
- * es_shard_signal and es_shard_wait are the two halves of es_shard_finish
- * (and es_shard_signal on the ready flag the first step of
+ *   es_shard_finish(slots[rank], slots, count, epoch)
+ *                                          stores this GPU's tag into its
+ *                                          slot of every GPU's slot array
+ *                                          and waits for every GPU's tag in
+ *                                          its own: afterwards every GPU's
+ *                                          outputs are complete and no GPU
+ *                                          reads this GPU's shard or buffers.
+ *                                          slots[g] is GPU g's array of
+ *                                          `count` 64-bit words (zeroed when
+ *                                          allocated), readable and writable
+ *                                          by every GPU.
+ * es_shard_signal and es_shard_wait raise one flag and wait for a set of
+ * flags (es_shard_signal on the ready flag is the first step of
  * es_verify_sharded), for a caller that runs several shards on one GPU and
- * must issue every shard's signal before any shard's wait.
+ * must issue every shard's signal before any shard's wait: a done flag per
+ * shard takes the place of the slot arrays there.
  * Every wait is bounded (about a second): a wait that gives up marks the
  * affected rows INVALID_INPUT (es_verify_sharded) or adds one to *timeouts
  * (es_shard_wait). */
@@ -215,7 +222,10 @@ int es_verify_sharded(const es_args* args, const es_shards* shards, void* stream
 int es_shard_signal(uint64_t* flag, uint64_t epoch, void* stream);
 /* Waits on the stream until every flags[i] (i < count) has reached `epoch`. */
 int es_shard_wait(const uint64_t* const* flags, int32_t count, uint64_t epoch, uint32_t* timeouts, void* stream);
-/* es_shard_signal(done, epoch) then es_shard_wait(flags, ...), as one launch. */
+/* This GPU's tag into slot `rank` of every GPU's slot array (rank: the
+ * index of `done`, this GPU's array, in `flags`, every GPU's), then a wait
+ * for every GPU's tag in `done`; one launch, which waits on the device for
+ * the stream's earlier kernels. */
 int es_shard_finish(uint64_t* done, const uint64_t* const* flags, int32_t count, uint64_t epoch, uint32_t* timeouts,
                     void* stream);
 /* Device memory other processes on this node can map: es_ipc_alloc returns a

@@ -137,5 +137,9 @@ def test_flag_and_ipc_entry_points_need_a_gpu():
     done = ctypes.cast(flag, ctypes.c_void_p)
     assert lib.es_shard_finish(done, flags, 1, 1, None, None) == -7
     assert lib.es_shard_finish(None, flags, 1, 1, None, None) == -1
+    # This GPU's slot array must be one of every GPU's slot arrays.
+    other = (ctypes.c_uint64 * 1)()
+    assert lib.es_shard_finish(ctypes.cast(other, ctypes.c_void_p), flags, 1, 1, None, None) == -1
+    assert b"slot arrays" in lib.es_last_error()
     ptr, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
     assert lib.es_ipc_alloc(1024, ctypes.byref(ptr), handle) == -7
